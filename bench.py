@@ -1,0 +1,475 @@
+"""Benchmark of the RockNPU MUL_MAT offload on B200.
+
+Default workload (the reference's headline metric):
+every MUL_MAT the ggml plugin offloads in one TinyLlama-1.1B-shaped Q4_K_M
+prefill of 512 tokens -- 22 layers x {QKV group (Q4_K 2048 + Q4_K 256 + Q6_K
+256), O (Q4_K 2048), gate+up group (2 x Q4_K 5632), down (k 5632 -> 2048,
+Q6_K in every other layer)}.  The vocabulary head (n = 32000) is not
+offloaded by the reference (n > 24576, ggml-rocknpu.cpp:648) and the
+attention / norm / RoPE work stays on llama.cpp's CPU backend, so neither is
+in a step.  Weights are random-init (N(0, 0.02^2) encoded to Q4_K/Q6_K),
+activations N(0, 1); prepared int8 weights are resident (the reference's
+weight cache), 1.0 GB per step > L2, so no extra L2 flush is needed.
+
+* value: tok/s with activations already in HBM (device entry points:
+  K2 per-token quantisation + K3 tcgen05 W8A8 GEMM per MUL_MAT).
+* e2e:   tok/s through the reference C ABI with pinned host buffers, as the
+  plugin calls it (rocknpu_matmul_q_concat_f32_f32_mtile for the groups,
+  rocknpu_matmul_q{4,6}_k_f32_f32 for O and down): H2D of every activation
+  and D2H of every output inside the timed region.
+* cpu_baseline / --impl reference: the reference's CPU path restated in C
+  (oracle/, OpenMP, all host threads): per-token quantisation, int32 GEMM,
+  rescale -- timed on a bounded sample of the same workload.
+
+Multi-GPU (torchrun): the path does not shard at this size, so each rank
+runs its own replica on its own prompt batch (weak scaling, no collective);
+value = all ranks' tokens / max-over-ranks time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+LAYERS = 22
+HIDDEN, FFN, KV = 2048, 5632, 256
+
+
+def layer_plan(layer: int):
+    """(name, [(kind, n)], k) of the four offloaded MUL_MAT calls of a layer."""
+    down_kind = 6 if layer % 2 == 0 else 4
+    return [("qkv", [(4, HIDDEN), (4, KV), (6, KV)], HIDDEN),
+            ("o", [(4, HIDDEN)], HIDDEN),
+            ("gate_up", [(4, FFN), (4, FFN)], HIDDEN),
+            ("down", [(down_kind, HIDDEN)], FFN)]
+
+
+def algorithmic(m: int):
+    """Bytes and int8 ops of the GEMM launches of one step (K3 only): int8
+    weights + int8 activations + f32 output + scales, and 2*m*n*k."""
+    b = ops = 0
+    for layer in range(LAYERS):
+        for _, members, k in layer_plan(layer):
+            n = sum(nn for _, nn in members)
+            b += n * k + m * k + 4 * m * n + 4 * n + 4 * m
+            ops += 2 * m * n * k
+    return b, ops
+
+
+def h2d_d2h_bytes(m: int):
+    h2d = d2h = 0
+    for layer in range(LAYERS):
+        for _, members, k in layer_plan(layer):
+            h2d += 4 * m * k
+            d2h += 4 * m * sum(nn for _, nn in members)
+    return h2d, d2h
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# workload construction
+# ---------------------------------------------------------------------------
+
+def make_weights(seed: int = 1000):
+    """Host K-quant blocks per layer and call: {(layer, call): [blocks...]}."""
+    import rocknpu_b200 as rk
+    weights = {}
+    s = seed
+    for layer in range(LAYERS):
+        for name, members, k in layer_plan(layer):
+            blocks = []
+            for kind, n in members:
+                blocks.append(rk.synth_q_weights(kind, n, k, seed=s, sigma=0.02))
+                s += 1
+            weights[(layer, name)] = blocks
+    return weights
+
+
+def make_activations(m: int, seed: int):
+    import rocknpu_b200 as rk
+    acts = {}
+    s = seed
+    for layer in range(LAYERS):
+        for name, _, k in layer_plan(layer):
+            acts[(layer, name)] = rk.synth_normal(s, m * k).reshape(m, k)
+            s += 1
+    return acts
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def run_ours(args, rank: int, world: int):
+    import torch
+    import rocknpu_b200 as rk
+    from rocknpu_b200 import device as dev
+
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+    rk.apply_default_env()
+    m = args.tokens
+    hbm_peak, bf16_peak, peak_src = load_peaks()
+    int8_peak_tops = 2.0 * bf16_peak  # dense int8 = 2x dense bf16 on B200
+
+    t0 = time.time()
+    weights = make_weights()
+    acts = make_activations(m, seed=5000 + 97 * rank)
+    gen_s = time.time() - t0
+
+    ctx = rk.Context()
+    stream = torch.cuda.current_stream()
+    status = dev.new_status()
+
+    # resident prepared weights (K1 on the GPU), concatenated per call
+    prepared = {}
+    for key, blocks in weights.items():
+        _, members, k = layer_plan(key[0])[["qkv", "o", "gate_up", "down"].index(key[1])]
+        ws, ss = [], []
+        for (kind, n), b in zip(members, blocks):
+            w8, s8 = dev.prepare_w8(kind, torch.from_numpy(b).cuda(), k, n, status)
+            ws.append(w8)
+            ss.append(s8)
+        prepared[key] = (torch.cat(ws).contiguous(), torch.cat(ss).contiguous(), k)
+    torch.cuda.synchronize()
+    assert status.item() == 0, "weight preparation failed"
+
+    d_acts = {key: torch.from_numpy(a).cuda() for key, a in acts.items()}
+    outs = {}
+    for key, (w8, s8, k) in prepared.items():
+        outs[key[1]] = torch.empty((m, w8.shape[0]), dtype=torch.float32, device="cuda")
+
+    def step():
+        for key, (w8, s8, k) in prepared.items():
+            dev.matmul_w8a8(ctx, d_acts[key], w8, s8, outs[key[1]], stream=stream)
+
+    launches_per_step = 2 * len(prepared)
+
+    dist = None
+    if world > 1:
+        import torch.distributed as dist_mod
+        dist = dist_mod
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if rk.lib().rocknpu_b200_context_check(ctx.handle) != 0:
+        raise RuntimeError("device status error during warm-up")
+
+    barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = start.elapsed_time(end) / args.steps
+    if rk.lib().rocknpu_b200_context_check(ctx.handle) != 0:
+        raise RuntimeError("device status error during timing")
+
+    # roofline: time the GEMM launches alone (same kernels, events per launch)
+    gemm_ms = 0.0
+    a8 = {}
+    for key, (w8, s8, k) in prepared.items():
+        q, s = dev.quantize_rows(d_acts[key], status)
+        a8[key] = (q, s)
+    torch.cuda.synchronize()
+    reps = 3
+    evs = []
+    for _ in range(reps):
+        for key, (w8, s8, k) in prepared.items():
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            dev.gemm_w8a8(a8[key][0], a8[key][1], w8, s8, status, out=outs[key[1]], stream=stream)
+            e1.record(stream)
+            evs.append((e0, e1))
+    torch.cuda.synchronize()
+    gemm_ms = sum(e0.elapsed_time(e1) for e0, e1 in evs) / reps
+    alg_bytes, alg_ops = algorithmic(m)
+    gb_s = alg_bytes / (gemm_ms * 1e-3) / 1e9
+    tops = alg_ops / (gemm_ms * 1e-3) / 1e12
+    t_hbm = alg_bytes / (hbm_peak * 1e9)
+    t_tc = alg_ops / (int8_peak_tops * 1e12)
+    if t_hbm >= t_tc:
+        roof = {"bound": "hbm", "achieved": round(gb_s, 1), "peak": hbm_peak, "unit": "GB/s",
+                "frac": round(gb_s / hbm_peak, 4)}
+    else:
+        roof = {"bound": "tensor", "achieved": round(tops, 1), "peak": int8_peak_tops, "unit": "TOP/s",
+                "frac": round(tops / int8_peak_tops, 4)}
+    roof.update({"kernel": "gemm_tc_kernel (K3, tcgen05 kind::i8)", "traffic": None,
+                 "peak_source": f"{peak_src} (int8 = 2 x bf16_tflops)" if roof["bound"] == "tensor"
+                 else f"{peak_src} hbm_gbs",
+                 "gemm_ms_per_step": round(gemm_ms, 4), "gemm_share_of_step": round(gemm_ms / ms, 3),
+                 "algorithmic_bytes_per_step": alg_bytes, "int8_ops_per_step": alg_ops})
+
+    # e2e through the reference C ABI with pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        h_acts = {key: torch.from_numpy(a).pin_memory() for key, a in acts.items()}
+        h_outs = {}
+        for key in prepared:
+            members = layer_plan(key[0])[["qkv", "o", "gate_up", "down"].index(key[1])][1]
+            h_outs[key] = [torch.empty((m, n), dtype=torch.float32).pin_memory() for _, n in members]
+
+        def e2e_step():
+            for key, blocks in weights.items():
+                _, members, k = layer_plan(key[0])[["qkv", "o", "gate_up", "down"].index(key[1])]
+                a = h_acts[key].numpy()
+                os_ = [o.numpy() for o in h_outs[key]]
+                if len(members) > 1:
+                    st = ctx.matmul_q_concat(blocks, [kd for kd, _ in members], [n for _, n in members], a, os_, m, k)
+                else:
+                    st = ctx.matmul_q(members[0][0], blocks[0], a, os_[0], m, k, members[0][1])
+                if st != 0:
+                    raise RuntimeError(f"C ABI call {key} failed: {st}")
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step()  # first pass also builds the resident weight caches
+        barrier()
+        e_steps = max(1, min(args.steps, 10))
+        t_start = time.perf_counter()
+        for _ in range(e_steps):
+            e2e_step()
+        e2e_s = (time.perf_counter() - t_start) / e_steps
+        if dist is not None:
+            t = torch.tensor([e2e_s], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_s = float(t.item())
+        h2d, d2h = h2d_d2h_bytes(m)
+        e2e = {"value": round(world * m / e2e_s, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_s * 1e3, 3),
+               "path": "rocknpu_matmul_q_concat_f32_f32_mtile + rocknpu_matmul_q{4,6}_k_f32_f32, pinned host"}
+
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(weights, acts, m, budget_s=args.cpu_seconds)
+
+    ctx.close()
+    if rank != 0:
+        return None
+    line = {
+        "metric": f"prefill tok/s pp{m} TinyLlama-shape Q4_K_M (ggml MUL_MAT offload)",
+        "value": round(world * m / (ms * 1e-3), 1),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int8 (W8A8, int32 accumulate, f32 out)",
+        "data": "synthetic (random-init N(0,0.02^2) -> Q4_K/Q6_K weights, N(0,1) activations)",
+        "config": {"workload": f"tinyllama-1.1b-q4_k_m-prefill-pp{m}-mul_mat", "tokens_per_step": m,
+                   "global_batch": world * m, "seq_len": m, "layers": LAYERS,
+                   "calls_per_step": len(prepared), "parallelism": f"replicas{world}",
+                   "l2": "inputs > L2: 0.97 GB resident int8 weights streamed per step"},
+        "roofline": roof,
+        "e2e": e2e,
+        "cpu_baseline": cpu,
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks.summary(),
+        "setup_s": round(gen_s, 1),
+    }
+    return line
+
+
+def cpu_baseline(weights, acts, m, budget_s=20.0):
+    """The reference's CPU path (oracle C port, OpenMP) on whole calls of the
+    workload until the time budget is spent; scaled to tok/s of a step."""
+    import oracle
+    prepared = []
+    for key, blocks in list(weights.items())[:8]:  # two layers' worth of calls
+        _, members, k = layer_plan(key[0])[["qkv", "o", "gate_up", "down"].index(key[1])]
+        ws, ss = [], []
+        for (kind, n), b in zip(members, blocks):
+            st, w, s = oracle.prepare_w8a8(kind, b, k, n)
+            ws.append(w)
+            ss.append(s)
+        prepared.append((key, np.concatenate(ws), np.concatenate(ss), k))
+    calls = 0
+    ops_done = 0
+    t0 = time.perf_counter()
+    while True:
+        for key, w, s, k in prepared:
+            st, _ = oracle.matmul_w8a8(w, s, acts[key])
+            calls += 1
+            ops_done += 2 * m * w.shape[0] * k
+            if time.perf_counter() - t0 > budget_s:
+                break
+        if time.perf_counter() - t0 > budget_s or calls >= 4 * len(prepared):
+            break
+    dt = time.perf_counter() - t0
+    _, step_ops = algorithmic(m)
+    step_s = dt * step_ops / ops_done
+    return {"value": round(m / step_s, 2), "unit": "tok/s", "cores": oracle.threads(), "kind": "port",
+            "sample": f"{calls} whole MUL_MAT calls of layers 0-1 (quantize + int32 GEMM + rescale, "
+                      f"prepared weights), {dt:.1f} s, scaled by int8 ops to one 22-layer step"}
+
+
+def run_reference(args, rank: int, world: int):
+    """--impl reference: the reference's CPU implementation of the path (the
+    oracle port; the Rust reference has no toolchain here) on the host cores."""
+    if rank != 0:
+        return None
+    import oracle
+    m = args.tokens
+    weights = make_weights()
+    acts = make_activations(m, seed=5000)
+    # prepared once (the reference caches prepared weights), like our arm
+    prepared = []
+    for key, blocks in weights.items():
+        _, members, k = layer_plan(key[0])[["qkv", "o", "gate_up", "down"].index(key[1])]
+        ws, ss = [], []
+        for (kind, n), b in zip(members, blocks):
+            st, w, s = oracle.prepare_w8a8(kind, b, k, n)
+            ws.append(w)
+            ss.append(s)
+        prepared.append((key, np.concatenate(ws), np.concatenate(ss), k))
+    # each step is a bounded sample: the calls of ONE layer, scaled to 22
+    sample = prepared[:4]
+
+    def step():
+        for key, w, s, k in sample:
+            oracle.matmul_w8a8(w, s, acts[key])
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    layer_s = (time.perf_counter() - t0) / args.steps
+    step_s = layer_s * LAYERS
+    value = round(m / step_s, 2)
+    line = {
+        "impl": "reference",
+        "metric": f"prefill tok/s pp{m} TinyLlama-shape Q4_K_M (ggml MUL_MAT offload)",
+        "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(step_s * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8 (W8A8, int32 accumulate, f32 out)", "data": "synthetic",
+        "config": {"workload": f"tinyllama-1.1b-q4_k_m-prefill-pp{m}-mul_mat", "tokens_per_step": m,
+                   "seq_len": m, "layers": LAYERS},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": oracle.threads(), "kind": "port",
+                         "sample": "each step times layer 0's four MUL_MAT calls (quantize + int32 GEMM + "
+                                   "rescale on prepared weights) and scales x22"},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--tokens", type=int, default=512)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world > 1 and args.impl == "ours":
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    try:
+        line = run_reference(args, rank, world) if args.impl == "reference" else run_ours(args, rank, world)
+    finally:
+        if world > 1 and args.impl == "ours":
+            import torch.distributed as dist
+            dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

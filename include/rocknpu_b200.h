@@ -1,0 +1,123 @@
+/*
+ * rocknpu_b200.h -- what librocknpu.so adds beside the reference C ABI
+ * (rocknpu.h).  Three groups:
+ *
+ *  1. The ggml plugin's host rules (adapters/ggml-rocknpu), exported so a
+ *     plugin built against ggml can call them and tests can check them
+ *     without ggml: the default route environment and the MUL_MAT
+ *     supports_op decision, over a plain description of the node.
+ *  2. Device-pointer ("resident") entry points: the same kernels as the
+ *     host-pointer ABI, for callers whose tensors already live in HBM
+ *     (multi-GPU N-sharding, graph capture, benchmarks).  Every pointer is
+ *     a device pointer on the context's GPU, work is queued on `stream`
+ *     (NULL = the context's own stream) and the call returns without
+ *     waiting.  Kernels report errors in the device word `status`
+ *     (0 = ok, 1 = non-finite input, >1 = a device-side wait ran out).
+ *  3. Synthetic K-quant weights for tests and benchmarks (host only).
+ */
+#ifndef ROCKNPU_B200_H
+#define ROCKNPU_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "rocknpu.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- 1. ggml plugin rules --------------------------------------------- */
+
+/* ggml type ids used by the rules (ggml's GGML_TYPE_* values). */
+enum rocknpu_ggml_type {
+    ROCKNPU_GGML_F32 = 0,
+    ROCKNPU_GGML_F16 = 1,
+    ROCKNPU_GGML_Q4_K = 12,
+    ROCKNPU_GGML_Q5_K = 13,
+    ROCKNPU_GGML_Q6_K = 14,
+};
+
+/* The parts of a ggml MUL_MAT node that supports_op reads: src0 = weights
+ * [ne0 = k, ne1 = n, ne2, ne3], src1 = activations [k, m, ...], dst. */
+typedef struct rocknpu_mul_mat_desc {
+    int32_t is_mul_mat;      /* node->op == GGML_OP_MUL_MAT with both sources */
+    int32_t weight_type;     /* src0->type */
+    int32_t act_type;        /* src1->type */
+    int32_t dst_type;        /* node->type */
+    int64_t weight_ne[4];
+    int64_t act_ne[4];
+    int32_t weight_contiguous;
+    int32_t act_contiguous;
+    int32_t dst_contiguous;
+} rocknpu_mul_mat_desc;
+
+/* Set the plugin's validated default routes (setenv without overwrite),
+ * as ggml_backend_rocknpu_reg does on registration
+ * (ggml-rocknpu.cpp:1859-1871). */
+void rocknpu_apply_default_env(void);
+
+/* 1 when the plugin claims the node, 0 otherwise: the decision of
+ * rocknpu_mul_mat_supported (ggml-rocknpu.cpp:614-715), environment
+ * switches included. */
+int rocknpu_mul_mat_supported(const rocknpu_mul_mat_desc *desc);
+
+/* ---- 2. device-pointer entry points ------------------------------------ */
+
+/* Opaque CUDA stream (cudaStream_t). */
+typedef void *rocknpu_stream;
+
+/* The context's own stream. */
+rocknpu_stream rocknpu_b200_context_stream(rocknpu_context *context);
+
+/* Wait for the context's stream and turn its device status word (written by
+ * rocknpu_b200_matmul_w8a8) into a status code, clearing it. */
+int rocknpu_b200_context_check(rocknpu_context *context);
+
+/* K1: Q4_K/Q5_K/Q6_K rows (kind 4/5/6, n rows of k values, k % 256 == 0) ->
+ * int8 rows w_i8[n][k] + scales[n], bit-identical to the reference's
+ * prepare_q*_k_w8a8 (capi/src/lib.rs:711-757, 974-994). */
+int rocknpu_b200_prepare_w8(uint32_t kind, const uint8_t *blocks, size_t k, size_t n, int8_t *w_i8, float *scales,
+                            int *status, rocknpu_stream stream);
+
+/* K2: per-token int8 a_i8[m][ld_i8] + scales[m]
+ * (quantize_symmetric_into per row, capi/src/lib.rs:614-654). */
+int rocknpu_b200_quantize_rows(const float *a, size_t m, size_t k, int8_t *a_i8, size_t ld_i8, float *scales,
+                               int *status, rocknpu_stream stream);
+
+/* K3: out[m][ldo] = (f32(acc) * a_scales[m]) * w_scales[n], acc = exact int32
+ * sum_k a_i8[m][k] * w_i8[n][k]; acc_out (optional, [m][n]) receives acc. */
+int rocknpu_b200_gemm_w8a8(const int8_t *a_i8, size_t ld_a, const float *a_scales, const int8_t *w_i8,
+                           size_t ld_w, const float *w_scales, float *out, size_t ldo, int32_t *acc_out, size_t m,
+                           size_t k, size_t n, int *status, rocknpu_stream stream);
+
+/* K2 + K3 (+ K5 for m == 1) through the context's workspace: the whole
+ * W8A8 MUL_MAT on resident f32 activations and resident prepared weights. */
+int rocknpu_b200_matmul_w8a8(rocknpu_context *context, const float *a, const int8_t *w_i8, const float *w_scales,
+                             float *out, size_t m, size_t k, size_t n, rocknpu_stream stream);
+
+/* K4: out[m][ldo] = sum_k f16(a)[m][k] * w_f16[n][k] in f32 on tcgen05;
+ * a_f16 row pitch ld_a elements (multiple of 8). */
+int rocknpu_b200_gemm_f16(const uint16_t *a_f16, size_t ld_a, const uint16_t *w_f16, size_t ld_w, float *out,
+                          size_t ldo, size_t m, size_t k, size_t n, int *status, rocknpu_stream stream);
+
+/* K5: M=1 W8A8 GEMV: out[n] = (f32(acc) * a_scale[0]) * w_scales[n]. */
+int rocknpu_b200_gemv_w8a8(const int8_t *a_i8, const float *a_scale, const int8_t *w_i8, const float *w_scales,
+                           float *out, size_t k, size_t n, rocknpu_stream stream);
+
+/* ---- 3. synthetic K-quant weights (host) ------------------------------- */
+
+/* Deterministic N(0, sigma^2) f32 values (counter-based: value i depends only
+ * on seed and i, so any slice can be generated independently). */
+void rocknpu_synth_normal(uint64_t seed, uint64_t first, size_t count, float sigma, float *out);
+
+/* Encode rows of f32 values (n rows of k, k % 256 == 0) as Q4_K (4), Q5_K (5)
+ * or Q6_K (6) superblocks: a simple min/max encoder producing valid blocks
+ * (any valid encoding is a valid input; parity starts at the block bytes). */
+int rocknpu_synth_encode(uint32_t kind, const float *values, size_t k, size_t n, uint8_t *blocks);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,1065 @@
+// The RockNPU C ABI (include/rocknpu.h) on B200.
+//
+// Host side of every entry point: argument validation in the reference's
+// order, the reference's route decision (which numerics a shape gets), the
+// resident-weight caches keyed like the reference's DecodeWeightKey
+// (address, bytes, k, n, kind; capi/src/lib.rs:33-39), and one CUDA stream
+// per context.  All arithmetic runs in the sm_100a kernels (kernels.h);
+// there is no CPU compute path.  Citations are file:line in the
+// darkautism/RockNPU tree; "L" is crates/rocknpu-capi/src/lib.rs.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <set>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/rocknpu.h"
+#include "../../include/rocknpu_b200.h"
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace {
+
+constexpr int kOk = ROCKNPU_STATUS_OK;
+constexpr int kInvalid = ROCKNPU_STATUS_INVALID_ARGUMENT;
+constexpr int kDeviceError = ROCKNPU_STATUS_DEVICE_ERROR;
+constexpr int kExecError = ROCKNPU_STATUS_EXECUTION_ERROR;
+
+// Kind tags of cached weights: the reference's K-quant kinds, plus the two
+// raw forms the W8 / FP16 entry points receive.
+constexpr int kKindW8 = 8;
+constexpr int kKindF16 = 16;
+
+// env_enabled (L:290-298): set, non-empty and not "0".
+bool env_enabled(const char* name) {
+    const char* v = std::getenv(name);
+    return v != nullptr && v[0] != '\0' && std::strcmp(v, "0") != 0;
+}
+
+// mtile_shape_enabled (L:330-344).
+bool mtile_shape_enabled(size_t k, size_t n) {
+    if (!env_enabled("ROCKNPU_W8_MTILE")) return false;
+    const char* scope = std::getenv("ROCKNPU_W8_MTILE_SCOPE");
+    if (scope == nullptr || scope[0] == '\0' || !std::strcmp(scope, "all")) return true;
+    if (!std::strcmp(scope, "kv")) return k == 2048 && n == 256;
+    if (!std::strcmp(scope, "qo")) return k == 2048 && n == 2048;
+    if (!std::strcmp(scope, "ffn")) return (k == 2048 && n == 5632) || (k == 5632 && n == 2048);
+    if (!std::strcmp(scope, "attn")) return k == 2048 && (n == 256 || n == 2048);
+    if (!std::strcmp(scope, "safe")) return k == 2048 && (n == 256 || n == 5632);
+    return false;
+}
+
+// native_mtile_routes_enabled (L:1998-2003).
+bool native_routes() {
+    return env_enabled("ROCKNPU_NATIVE_MTILE") && env_enabled("ROCKNPU_MTILE_PERSIST") &&
+           env_enabled("ROCKNPU_W8_MTILE") && env_enabled("ROCKNPU_MTILE_MC");
+}
+
+bool mtile_rows(size_t m) {  // MTILE_ROWS (L:1992)
+    return m == 4 || m == 8 || m == 12 || m == 16 || m == 32 || m == 48 || m == 64 || m == 128;
+}
+
+size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Column chunk width of split_wide_mtile (L:2140-2141) for n > 8192.
+size_t wide_chunk(size_t n) {
+    const size_t chunks = (n + 8191) / 8192;
+    return ((n / 32 + chunks - 1) / chunks) * 32;
+}
+
+enum class Route { W8A8, FP16, Invalid };
+
+// Which numerics rocknpu_matmul_q{4,6}_k_f32_f32 (L:4933-5256, 5380-5671)
+// gives an M>1 call.  Every W8A8 branch of the reference (row tiles, 64-row
+// halves, column chunks, K zero-padding, K- or N-split across cores) yields
+// the same per-element result -- per-row int8 weights, per-token int8
+// activations, exact int32 sums, (f32(acc)*a_s)*w_s -- so only the branch
+// family matters.  Shapes no W8A8 branch accepts take the FP16 route
+// (execute_cached_prefill / the uncached FP16 bridge: f16 weights and
+// activations, f32 accumulation).
+Route route_q46_prompt(size_t m, size_t k, size_t n) {
+    const bool native = native_routes();
+    const bool NATIVE = env_enabled("ROCKNPU_NATIVE_MTILE"), PERSIST = env_enabled("ROCKNPU_MTILE_PERSIST"),
+               MC = env_enabled("ROCKNPU_MTILE_MC"), DOWN = env_enabled("ROCKNPU_NATIVE_MTILE_DOWN");
+    size_t nc = n;
+    size_t mt = m;
+    if (native) {
+        if (n > 8192 && n % 32 == 0) nc = wide_chunk(n);  // split_wide_mtile (L:2136-2160)
+        if (!mtile_rows(m)) mt = 128;                      // run_mtile_row_chunks (L:2216-2256)
+        if (mt == 128 && round_up(k, 512) > 2048 && !(round_up(k, 512) > 4096 && round_up(k, 512) <= 6144))
+            mt = 64;                                       // 64-row halves (L:2110-2128)
+    } else if (!mtile_rows(m)) {
+        return Route::FP16;
+    }
+    const size_t kp = round_up(k, 512);
+    const bool ncols = nc % 32 == 0 && nc <= 8192;
+    // padded-K route (L:5031-5048)
+    if (native && DOWN && k % 512 != 0 && kp <= 3 * 4096 && ncols) return Route::W8A8;
+    // K-split route (L:5050-5075)
+    if (k > 4096 && k <= 3 * 4096 && k % 512 == 0 && ncols && NATIVE && DOWN && PERSIST && MC &&
+        mtile_shape_enabled(k, nc))
+        return Route::W8A8;
+    // N-split / single-core route (L:5077-5105)
+    if (mt != 16 && NATIVE && PERSIST && k <= 4096 && k % 512 == 0 && ncols && mtile_shape_enabled(k, nc))
+        return Route::W8A8;
+    // M=16 route (L:5107-5148)
+    if (mt == 16 && k <= 4096 && k % 512 == 0 && ncols && mtile_shape_enabled(k, nc)) return Route::W8A8;
+    return Route::FP16;
+}
+
+// rocknpu_matmul_q5_k_f32_f32 (L:5270-5378): W8A8 or nothing.
+Route route_q5_prompt(size_t m, size_t k, size_t n) {
+    const bool native = native_routes();
+    size_t nc = n;
+    if (native) {
+        if (n > 8192 && n % 32 == 0) nc = wide_chunk(n);
+    } else if (!mtile_rows(m)) {
+        return Route::Invalid;
+    }
+    if (env_enabled("ROCKNPU_NATIVE_MTILE") && env_enabled("ROCKNPU_MTILE_PERSIST") && k <= 4096 && k % 512 == 0 &&
+        nc % 32 == 0 && nc <= 8192 && mtile_shape_enabled(k, nc))
+        return Route::W8A8;
+    return Route::Invalid;
+}
+
+// ---- device memory ---------------------------------------------------------
+
+struct DevBuf {
+    void* ptr = nullptr;
+    size_t cap = 0;
+    cudaError_t ensure(size_t bytes) {
+        if (bytes <= cap) return cudaSuccess;
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        cap = 0;
+        const size_t want = std::max(bytes, round_up(bytes + bytes / 4, 1 << 20));
+        cudaError_t e = cudaMalloc(&ptr, want);
+        if (e != cudaSuccess) {
+            ptr = nullptr;
+            return e;
+        }
+        cap = want;
+        return cudaSuccess;
+    }
+    void release() {
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        cap = 0;
+    }
+    template <class T>
+    T* as() const {
+        return static_cast<T*>(ptr);
+    }
+};
+
+// Resident prepared int8 rows [n][k] + per-row scales [n].
+struct PreparedW8 {
+    int8_t* w = nullptr;
+    float* scales = nullptr;
+    size_t n = 0, k = 0;
+    std::vector<size_t> member_n;  // concatenated groups: rows per member
+    ~PreparedW8() {
+        if (w) cudaFree(w);
+        if (scales) cudaFree(scales);
+    }
+    size_t bytes() const { return n * k + n * sizeof(float); }
+};
+
+// Resident f16 rows [n][ld].
+struct PreparedF16 {
+    __half* w = nullptr;
+    size_t n = 0, k = 0, ld = 0;
+    ~PreparedF16() {
+        if (w) cudaFree(w);
+    }
+    size_t bytes() const { return n * ld * sizeof(__half); }
+};
+
+struct Key {
+    uintptr_t address;
+    size_t bytes, k, n;
+    int kind;
+    bool operator<(const Key& o) const {
+        return std::tie(address, bytes, k, n, kind) < std::tie(o.address, o.bytes, o.k, o.n, o.kind);
+    }
+    bool operator==(const Key& o) const {
+        return address == o.address && bytes == o.bytes && k == o.k && n == o.n && kind == o.kind;
+    }
+};
+
+using KeyList = std::vector<Key>;
+using W8Ptr = std::shared_ptr<PreparedW8>;
+using F16Ptr = std::shared_ptr<PreparedF16>;
+
+uint64_t now_ns() {
+    return static_cast<uint64_t>(
+        std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now().time_since_epoch())
+            .count());
+}
+
+}  // namespace
+
+struct RockNpuContext {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    bool direct_submit = false;  // ROCKNPU_W8_DIRECT_SUBMIT at creation (int8_decode_pool.rs:509)
+
+    int* d_status = nullptr;  // device error word
+    int* h_status = nullptr;  // pinned mirror
+
+    DevBuf a_f32, a_i8, a_scale, a_f16, out_f32, staging, swiglu_tmp;
+
+    // Prompt-path (M-tile) resident weights: single projections and
+    // concatenated same-input groups (L:1808-1849, L:2351-2384).
+    std::map<Key, W8Ptr> mtile;
+    std::map<KeyList, W8Ptr> groups;
+    // Decode (M=1) resident weights: single, pair, triple (L:1605-1650,
+    // L:3264-3600).
+    std::map<Key, W8Ptr> decode;
+    std::map<KeyList, W8Ptr> decode_groups;
+    // FP16 executor weights and the FP16 route's dequantised weights.
+    std::map<Key, F16Ptr> f16;
+
+    // decode-cache statistics (rocknpu_decode_cache_stats)
+    size_t hits = 0, misses = 0;
+    uint64_t hit_ns = 0, miss_ns = 0;
+    size_t m1_calls = 0;
+    std::set<std::pair<size_t, size_t>> m1_shapes;
+
+    // prompt-path profile (ROCKNPU_MTILE_PROFILE, L:3900-3996)
+    bool profile = false;
+    size_t mtile_calls = 0, mtile_hits = 0, mtile_misses = 0;
+    uint64_t mtile_ns = 0, prepare_ns = 0;
+
+    rocknpu_overlap_fn overlap = nullptr;
+    void* overlap_user = nullptr;
+};
+
+namespace {
+
+using Ctx = RockNpuContext;
+
+int cuda_status(cudaError_t e) { return e == cudaSuccess ? kOk : kExecError; }
+
+// Wait for the stream, then map the device error word to a status.
+int finish(Ctx* c) {
+    cudaError_t e = cudaMemcpyAsync(c->h_status, c->d_status, sizeof(int), cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) return kExecError;
+    const int s = *c->h_status;
+    if (s == rk::kErrNone) return kOk;
+    return s == rk::kErrNonFinite ? kInvalid : kExecError;
+}
+
+int reset_status(Ctx* c) { return cuda_status(cudaMemsetAsync(c->d_status, 0, sizeof(int), c->stream)); }
+
+// Dequantise + requantise host K-quant rows into w/scales (device), rows of
+// one member of a (possibly concatenated) prepared weight.
+int prepare_member(Ctx* c, int kind, const uint8_t* host, size_t bytes, size_t k, size_t n, int8_t* w,
+                   float* scales) {
+    const size_t bb = rk::qblock_bytes(kind);
+    if (bb == 0 || k == 0 || n == 0 || k % 256 != 0 || bytes != n * (k / 256) * bb) return kInvalid;
+    if (c->staging.ensure(bytes) != cudaSuccess) return kExecError;
+    if (cudaMemcpyAsync(c->staging.ptr, host, bytes, cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
+        return kExecError;
+    rk::launch_prep_w8(kind, c->staging.as<uint8_t>(), static_cast<int>(k), static_cast<int>(n), w, scales,
+                       c->d_status, c->stream);
+    return cuda_status(cudaGetLastError());
+}
+
+struct Member {
+    int kind;
+    const uint8_t* host;  // K-quant bytes, or int8 rows for kKindW8
+    const float* host_scales;  // kKindW8 only
+    size_t bytes, n;
+};
+
+// Build one resident int8 weight from 1..4 members concatenated along N.
+int build_w8(Ctx* c, const Member* members, size_t count, size_t k, W8Ptr& out) {
+    auto p = std::make_shared<PreparedW8>();
+    size_t total = 0;
+    for (size_t i = 0; i < count; ++i) total += members[i].n;
+    p->n = total;
+    p->k = k;
+    if (cudaMalloc(&p->w, total * k) != cudaSuccess || cudaMalloc(&p->scales, total * sizeof(float)) != cudaSuccess)
+        return kExecError;
+    int st = reset_status(c);
+    if (st != kOk) return st;
+    size_t row = 0;
+    for (size_t i = 0; i < count && st == kOk; ++i) {
+        const Member& mb = members[i];
+        if (mb.kind == kKindW8) {
+            if (cudaMemcpyAsync(p->w + row * k, mb.host, mb.n * k, cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
+                cudaMemcpyAsync(p->scales + row, mb.host_scales, mb.n * sizeof(float), cudaMemcpyHostToDevice,
+                                c->stream) != cudaSuccess)
+                st = kExecError;
+        } else {
+            st = prepare_member(c, mb.kind, mb.host, mb.bytes, k, mb.n, p->w + row * k, p->scales + row);
+            // the staging buffer is reused by the next member: finish this one
+            if (st == kOk && i + 1 < count) st = cuda_status(cudaStreamSynchronize(c->stream));
+        }
+        p->member_n.push_back(mb.n);
+        row += mb.n;
+    }
+    if (st == kOk) st = finish(c);
+    if (st != kOk) return st;
+    out = std::move(p);
+    return kOk;
+}
+
+struct OutSeg {
+    float* host;  // [m][n] host output of one member
+    size_t n;
+};
+
+// Queue quantisation + GEMM (or GEMV for m == 1) of host activations
+// against a resident int8 weight, then copy the member outputs back.
+int run_w8a8(Ctx* c, const PreparedW8& pw, const float* host_a, size_t m, size_t k, const OutSeg* segs, size_t nseg,
+             bool m1_overlap) {
+    const size_t ld8 = round_up(k, 16);
+    const size_t total_n = pw.n;
+    if (c->a_f32.ensure(m * k * sizeof(float)) || c->a_i8.ensure(m * ld8) || c->a_scale.ensure(m * sizeof(float)) ||
+        c->out_f32.ensure(m * total_n * sizeof(float)))
+        return kExecError;
+    int st = reset_status(c);
+    if (st != kOk) return st;
+    if (cudaMemcpyAsync(c->a_f32.ptr, host_a, m * k * sizeof(float), cudaMemcpyHostToDevice, c->stream))
+        return kExecError;
+    rk::launch_quant_rows(c->a_f32.as<float>(), static_cast<int>(m), static_cast<int>(k), static_cast<long long>(k),
+                          c->a_i8.as<int8_t>(), static_cast<long long>(ld8), c->a_scale.as<float>(), c->d_status,
+                          c->stream);
+    float* out = c->out_f32.as<float>();
+    if (m == 1 && k % 16 == 0) {
+        rk::launch_gemv_w8a8(pw.w, pw.scales, c->a_i8.as<int8_t>(), c->a_scale.as<float>(), static_cast<int>(k),
+                             static_cast<int>(total_n), out, c->stream);
+        if (cudaGetLastError() != cudaSuccess) return kExecError;
+    } else {
+        rk::OutMembers om;
+        om.count = static_cast<int>(nseg);
+        size_t start = 0;
+        for (size_t i = 0; i < nseg; ++i) {
+            om.n_start[i] = static_cast<int>(start);
+            om.out[i] = out + m * start;
+            om.ldo[i] = static_cast<long long>(segs[i].n);
+            start += segs[i].n;
+        }
+        om.n_start[nseg] = static_cast<int>(start);
+        const int e = rk::launch_gemm_tc(0, pw.w, static_cast<long long>(pw.k), c->a_i8.ptr,
+                                         static_cast<long long>(ld8), static_cast<int>(m), static_cast<int>(total_n),
+                                         static_cast<int>(k), pw.scales, c->a_scale.as<float>(), om, nullptr, 0,
+                                         c->d_status, c->stream);
+        if (e != cudaSuccess) return kExecError;
+    }
+    if (m1_overlap && c->overlap) {
+        // one-shot host work while the GPU runs (take_overlap, L:264-273)
+        rocknpu_overlap_fn fn = c->overlap;
+        void* user = c->overlap_user;
+        c->overlap = nullptr;
+        c->overlap_user = nullptr;
+        fn(user);
+    }
+    st = finish(c);
+    if (st != kOk) return st;
+    size_t start = 0;
+    for (size_t i = 0; i < nseg; ++i) {
+        if (cudaMemcpyAsync(segs[i].host, out + m * start, m * segs[i].n * sizeof(float), cudaMemcpyDeviceToHost,
+                            c->stream))
+            return kExecError;
+        start += segs[i].n;
+    }
+    return cuda_status(cudaStreamSynchronize(c->stream));
+}
+
+// FP16 executor on resident f16 rows: f16(a) . w^T in f32.
+int run_f16(Ctx* c, const PreparedF16& pw, const float* host_a, size_t m, size_t k, float* host_out) {
+    const size_t ldh = round_up(k, 8);
+    const size_t n = pw.n;
+    if (c->a_f32.ensure(m * k * sizeof(float)) || c->a_f16.ensure(m * ldh * sizeof(__half)) ||
+        c->out_f32.ensure(m * n * sizeof(float)))
+        return kExecError;
+    int st = reset_status(c);
+    if (st != kOk) return st;
+    if (cudaMemcpyAsync(c->a_f32.ptr, host_a, m * k * sizeof(float), cudaMemcpyHostToDevice, c->stream))
+        return kExecError;
+    rk::launch_f32_to_f16(c->a_f32.as<float>(), static_cast<int>(m), static_cast<int>(k), static_cast<long long>(k),
+                          c->a_f16.as<__half>(), static_cast<long long>(ldh), c->stream);
+    rk::OutMembers om;
+    om.count = 1;
+    om.n_start[1] = static_cast<int>(n);
+    om.out[0] = c->out_f32.as<float>();
+    om.ldo[0] = static_cast<long long>(n);
+    const int e = rk::launch_gemm_tc(1, pw.w, static_cast<long long>(pw.ld * 2), c->a_f16.ptr,
+                                     static_cast<long long>(ldh * 2), static_cast<int>(m), static_cast<int>(n),
+                                     static_cast<int>(k), nullptr, nullptr, om, nullptr, 0, c->d_status, c->stream);
+    if (e != cudaSuccess) return kExecError;
+    st = finish(c);
+    if (st != kOk) return st;
+    if (cudaMemcpyAsync(host_out, c->out_f32.ptr, m * n * sizeof(float), cudaMemcpyDeviceToHost, c->stream))
+        return kExecError;
+    return cuda_status(cudaStreamSynchronize(c->stream));
+}
+
+// Resident f16 weights from a host K-quant tensor (the FP16 route's
+// dequantize_q*_k_prefill_f16, L:393-455).
+int build_f16_from_q(Ctx* c, int kind, const uint8_t* host, size_t bytes, size_t k, size_t n, F16Ptr& out) {
+    auto p = std::make_shared<PreparedF16>();
+    p->n = n;
+    p->k = k;
+    p->ld = k;  // k % 256 == 0
+    if (cudaMalloc(&p->w, n * k * sizeof(__half)) != cudaSuccess) return kExecError;
+    if (c->staging.ensure(bytes) || cudaMemcpyAsync(c->staging.ptr, host, bytes, cudaMemcpyHostToDevice, c->stream))
+        return kExecError;
+    rk::launch_dequant_f16(kind, c->staging.as<uint8_t>(), static_cast<int>(k), static_cast<int>(n), p->w,
+                           static_cast<long long>(k), c->d_status, c->stream);
+    if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(c->stream) != cudaSuccess) return kExecError;
+    out = std::move(p);
+    return kOk;
+}
+
+int build_f16_raw(Ctx* c, const uint16_t* host, size_t k, size_t n, F16Ptr& out) {
+    auto p = std::make_shared<PreparedF16>();
+    p->n = n;
+    p->k = k;
+    p->ld = round_up(k, 8);
+    if (cudaMalloc(&p->w, n * p->ld * sizeof(__half)) != cudaSuccess) return kExecError;
+    if (p->ld != k && cudaMemsetAsync(p->w, 0, n * p->ld * sizeof(__half), c->stream)) return kExecError;
+    if (cudaMemcpy2DAsync(p->w, p->ld * sizeof(__half), host, k * sizeof(__half), k * sizeof(__half), n,
+                          cudaMemcpyHostToDevice, c->stream))
+        return kExecError;
+    if (cudaStreamSynchronize(c->stream) != cudaSuccess) return kExecError;
+    out = std::move(p);
+    return kOk;
+}
+
+Key make_key(const void* p, size_t bytes, size_t k, size_t n, int kind) {
+    return Key{reinterpret_cast<uintptr_t>(p), bytes, k, n, kind};
+}
+
+bool bind(Ctx* c) { return cudaSetDevice(c->device) == cudaSuccess; }
+
+// Prompt-path single projection with K-quant weights (every W8A8 branch of
+// L:4933-5256).
+int q_prompt_w8a8(Ctx* c, int kind, const uint8_t* w, size_t bytes, const float* a, float* out, size_t m, size_t k,
+                  size_t n) {
+    const uint64_t t0 = c->profile ? now_ns() : 0;
+    const Key key = make_key(w, bytes, k, n, kind);
+    auto it = c->mtile.find(key);
+    if (it == c->mtile.end()) {
+        W8Ptr p;
+        const uint64_t p0 = c->profile ? now_ns() : 0;
+        Member mb{kind, w, nullptr, bytes, n};
+        const int st = build_w8(c, &mb, 1, k, p);
+        if (st != kOk) return st;
+        if (c->profile) c->prepare_ns += now_ns() - p0;
+        it = c->mtile.emplace(key, std::move(p)).first;
+        c->mtile_misses++;
+    } else {
+        c->mtile_hits++;
+    }
+    OutSeg seg{out, n};
+    const int st = run_w8a8(c, *it->second, a, m, k, &seg, 1, false);
+    if (c->profile) {
+        c->mtile_calls++;
+        c->mtile_ns += now_ns() - t0;
+    }
+    return st;
+}
+
+int q_prompt_f16(Ctx* c, int kind, const uint8_t* w, size_t bytes, const float* a, float* out, size_t m, size_t k,
+                 size_t n) {
+    const Key key = make_key(w, bytes, k, n, kind);
+    F16Ptr p;
+    auto it = c->f16.find(key);
+    if (it != c->f16.end()) {
+        p = it->second;
+    } else {
+        const int st = build_f16_from_q(c, kind, w, bytes, k, n, p);
+        if (st != kOk) return st;
+        // execute_cached_prefill keeps the weights only under
+        // ROCKNPU_PREFILL_CACHE; the uncached bridge re-decodes per call.
+        if (env_enabled("ROCKNPU_PREFILL_CACHE")) c->f16.emplace(key, p);
+    }
+    return run_f16(c, *p, a, m, k, out);
+}
+
+// M=1 through the decode cache (execute_cached_w8a8_m1, L:1567-1701 and the
+// pair/triple forms, L:3264-3600); `members` are concatenated along N.
+int decode_m1(Ctx* c, const KeyList& keys, const Member* members, size_t count, const float* a, OutSeg* segs,
+              size_t k) {
+    const uint64_t t0 = now_ns();
+    W8Ptr p;
+    bool hit = false;
+    if (count == 1) {
+        auto it = c->decode.find(keys[0]);
+        if (it != c->decode.end()) {
+            p = it->second;
+            hit = true;
+        }
+    } else {
+        auto it = c->decode_groups.find(keys);
+        if (it != c->decode_groups.end()) {
+            p = it->second;
+            hit = true;
+        }
+    }
+    if (!hit) {
+        const int st = build_w8(c, members, count, k, p);
+        if (st != kOk) return st;
+        if (count == 1)
+            c->decode.emplace(keys[0], p);
+        else
+            c->decode_groups.emplace(keys, p);
+        size_t total = 0;
+        for (size_t i = 0; i < count; ++i) total += members[i].n;
+        c->m1_shapes.insert({k, total});
+    }
+    const int st = run_w8a8(c, *p, a, 1, k, segs, count, true);
+    if (st != kOk) return st;
+    const uint64_t dt = now_ns() - t0;
+    c->m1_calls++;
+    if (hit) {
+        c->hits++;
+        c->hit_ns += dt;
+    } else {
+        c->misses++;
+        c->miss_ns += dt;
+    }
+    return kOk;
+}
+
+bool scales_valid(const float* s, size_t n) {
+    for (size_t i = 0; i < n; ++i)
+        if (!std::isfinite(s[i]) || s[i] <= 0.0f) return false;
+    return true;
+}
+
+bool mul_overflows(size_t a, size_t b, size_t* out) { return __builtin_mul_overflow(a, b, out); }
+
+// Shared body of rocknpu_matmul_q{4,5,6}_k_f32_f32.
+int matmul_q(Ctx* c, int kind, const uint8_t* w, size_t bytes, const float* a, float* out, size_t m, size_t k,
+             size_t n) {
+    if (!c || !w || !a || !out || m == 0 || k == 0 || n == 0 || k % 256 != 0) return kInvalid;
+    size_t a_len, out_len, blocks, expect;
+    if (mul_overflows(m, k, &a_len) || mul_overflows(m, n, &out_len) || mul_overflows(n, k / 256, &blocks) ||
+        mul_overflows(blocks, rk::qblock_bytes(kind), &expect) || bytes != expect)
+        return kInvalid;
+    if (!bind(c)) return kDeviceError;
+    if (kind == rk::kQ5K) {
+        if (m == 1) return kInvalid;  // L:5303-5305
+        return route_q5_prompt(m, k, n) == Route::W8A8 ? q_prompt_w8a8(c, kind, w, bytes, a, out, m, k, n) : kInvalid;
+    }
+    if (m == 1) {
+        // execute_cached_w8a8_m1's shape checks (L:1578-1585)
+        if (k % 512 != 0 || n % 32 != 0 || n > 8192) return kInvalid;
+        const Key key = make_key(w, bytes, k, n, kind);
+        Member mb{kind, w, nullptr, bytes, n};
+        OutSeg seg{out, n};
+        return decode_m1(c, KeyList{key}, &mb, 1, a, &seg, k);
+    }
+    switch (route_q46_prompt(m, k, n)) {
+        case Route::W8A8: return q_prompt_w8a8(c, kind, w, bytes, a, out, m, k, n);
+        case Route::FP16: return q_prompt_f16(c, kind, w, bytes, a, out, m, k, n);
+        default: return kInvalid;
+    }
+}
+
+int quant_kind46(uint32_t kind) { return kind == 4 ? rk::kQ4K : kind == 6 ? rk::kQ6K : 0; }
+
+// Concatenated-N prompt group (execute_cached_w8a8_mtile_concat, L:2262-2424):
+// one GEMM over the group's resident rows, member outputs split by column.
+int concat_group(Ctx* c, size_t count, const uint8_t* const* weights, const size_t* bytes, const int* kinds,
+                 const size_t* ns, const float* a, float* const* outs, size_t m, size_t k) {
+    KeyList keys;
+    std::vector<Member> members;
+    std::vector<OutSeg> segs;
+    size_t total = 0;
+    for (size_t i = 0; i < count; ++i) {
+        keys.push_back(make_key(weights[i], bytes[i], k, ns[i], kinds[i]));
+        members.push_back(Member{kinds[i], weights[i], nullptr, bytes[i], ns[i]});
+        segs.push_back(OutSeg{outs[i], ns[i]});
+        total += ns[i];
+    }
+    auto it = c->groups.find(keys);
+    if (it == c->groups.end()) {
+        W8Ptr p;
+        const int st = build_w8(c, members.data(), count, k, p);
+        if (st != kOk) return st;
+        it = c->groups.emplace(keys, std::move(p)).first;
+        c->mtile_misses++;
+    } else {
+        c->mtile_hits++;
+    }
+    return run_w8a8(c, *it->second, a, m, k, segs.data(), count, false);
+}
+
+}  // namespace
+
+// ============================================================================
+// C ABI
+// ============================================================================
+
+extern "C" {
+
+size_t rocknpu_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+    size_t usable = 0;
+    for (int d = 0; d < n; ++d) {
+        int major = 0;
+        if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, d) == cudaSuccess && major == 10)
+            ++usable;
+    }
+    return usable;
+}
+
+rocknpu_context* rocknpu_context_create(void) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    int major = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess || major != 10)
+        return nullptr;
+    auto* c = new (std::nothrow) RockNpuContext();
+    if (!c) return nullptr;
+    c->device = dev;
+    c->direct_submit = std::getenv("ROCKNPU_W8_DIRECT_SUBMIT") != nullptr;
+    c->profile = env_enabled("ROCKNPU_MTILE_PROFILE");
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc(&c->d_status, sizeof(int)) != cudaSuccess ||
+        cudaHostAlloc(&c->h_status, sizeof(int), cudaHostAllocDefault) != cudaSuccess ||
+        cudaMemset(c->d_status, 0, sizeof(int)) != cudaSuccess) {
+        rocknpu_context_destroy(c);
+        return nullptr;
+    }
+    return c;
+}
+
+int rocknpu_context_decode_cache_stats(const rocknpu_context* context, rocknpu_decode_cache_stats* out) {
+    if (!context || !out) return kInvalid;
+    const Ctx* c = context;
+    size_t resident = 0;
+    for (auto& kv : c->decode) resident += kv.second->bytes();
+    for (auto& kv : c->decode_groups) resident += kv.second->bytes();
+    rocknpu_decode_cache_stats s{};
+    s.hits = c->hits;
+    s.misses = c->misses;
+    s.entries = c->decode.size() + c->decode_groups.size();
+    s.resident_bytes = resident;
+    s.hit_ns = c->hit_ns;
+    s.miss_ns = c->miss_ns;
+    s.tuned_shapes = c->m1_shapes.size();
+    s.worker1_calls = c->m1_calls;
+    s.worker2_calls = 0;
+    s.worker3_calls = 0;
+    s.ksplit_calls = 0;
+    *out = s;
+    return kOk;
+}
+
+void rocknpu_context_destroy(rocknpu_context* context) {
+    if (!context) return;
+    Ctx* c = context;
+    cudaSetDevice(c->device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    if (c->profile) {
+        std::fprintf(stderr,
+                     "ROCKNPU MTILE PROFILE calls=%zu cache_hits=%zu cache_misses=%zu total_ms=%.3f "
+                     "weight_prepare_ms=%.3f\n",
+                     c->mtile_calls, c->mtile_hits, c->mtile_misses, c->mtile_ns / 1e6, c->prepare_ns / 1e6);
+    }
+    c->mtile.clear();
+    c->groups.clear();
+    c->decode.clear();
+    c->decode_groups.clear();
+    c->f16.clear();
+    for (DevBuf* b : {&c->a_f32, &c->a_i8, &c->a_scale, &c->a_f16, &c->out_f32, &c->staging, &c->swiglu_tmp})
+        b->release();
+    if (c->d_status) cudaFree(c->d_status);
+    if (c->h_status) cudaFreeHost(c->h_status);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+int rocknpu_context_set_overlap(rocknpu_context* context, rocknpu_overlap_fn callback, void* user_data) {
+    if (!context) return kInvalid;
+    context->overlap = callback;
+    context->overlap_user = callback ? user_data : nullptr;
+    return kOk;
+}
+
+int rocknpu_matmul_q4_k_f32_f32(rocknpu_context* context, const uint8_t* weights, size_t weights_bytes,
+                                const float* a, float* out, size_t m, size_t k, size_t n) {
+    return matmul_q(context, rk::kQ4K, weights, weights_bytes, a, out, m, k, n);
+}
+
+int rocknpu_matmul_q5_k_f32_f32(rocknpu_context* context, const uint8_t* weights, size_t weights_bytes,
+                                const float* a, float* out, size_t m, size_t k, size_t n) {
+    return matmul_q(context, rk::kQ5K, weights, weights_bytes, a, out, m, k, n);
+}
+
+int rocknpu_matmul_q6_k_f32_f32(rocknpu_context* context, const uint8_t* weights, size_t weights_bytes,
+                                const float* a, float* out, size_t m, size_t k, size_t n) {
+    return matmul_q(context, rk::kQ6K, weights, weights_bytes, a, out, m, k, n);
+}
+
+int rocknpu_matmul_q_concat_f32_f32_mtile(rocknpu_context* context, size_t count, const uint8_t* const* weights,
+                                          const size_t* bytes, const uint32_t* kinds, const size_t* ns,
+                                          const float* a, float* const* outputs, size_t m, size_t k) {
+    // argument checks of L:2469-2482 and execute_cached_w8a8_mtile_concat's
+    // shape checks (L:2272-2298); rows are independent, so the reference's
+    // 128-row tiles and 64-row halves need no split here.
+    if (!context || count < 1 || count > 4 || !weights || !bytes || !kinds || !ns || !a || !outputs || m == 0 ||
+        k == 0)
+        return kInvalid;
+    int kd[4];
+    size_t total = 0;
+    for (size_t i = 0; i < count; ++i) {
+        if (!weights[i] || !outputs[i] || ns[i] == 0) return kInvalid;
+        kd[i] = quant_kind46(kinds[i]);
+        if (!kd[i]) return kInvalid;
+        if (ns[i] % 32 != 0) return kInvalid;
+        total += ns[i];
+    }
+    if (!context->direct_submit || k % 512 != 0 || k > 4096 || total < 96 || total > 3 * 8192) return kInvalid;
+    for (size_t i = 0; i < count; ++i)
+        if (bytes[i] != ns[i] * (k / 256) * rk::qblock_bytes(kd[i])) return kInvalid;
+    if (!bind(context)) return kDeviceError;
+    return concat_group(context, count, weights, bytes, kd, ns, a, outputs, m, k);
+}
+
+int rocknpu_mtile_release(rocknpu_context* context, size_t count, const uint8_t* const* weights) {
+    if (!context || !weights || count < 1 || count > 4) return kInvalid;
+    std::vector<uintptr_t> addr(count);
+    for (size_t i = 0; i < count; ++i) addr[i] = reinterpret_cast<uintptr_t>(weights[i]);
+    auto involved = [&](const Key& k) { return std::find(addr.begin(), addr.end(), k.address) != addr.end(); };
+    if (!bind(context)) return kDeviceError;
+    cudaStreamSynchronize(context->stream);
+    for (auto it = context->mtile.begin(); it != context->mtile.end();)
+        it = involved(it->first) ? context->mtile.erase(it) : std::next(it);
+    for (auto it = context->groups.begin(); it != context->groups.end();) {
+        const KeyList& keys = it->first;
+        bool exact = keys.size() == count;
+        for (size_t i = 0; exact && i < count; ++i) exact = keys[i].address == addr[i];
+        bool any = false;
+        for (const Key& k : keys) any |= involved(k);
+        it = (!exact && any) ? context->groups.erase(it) : std::next(it);
+    }
+    return kOk;
+}
+
+int rocknpu_prewarm_quantized_m16(rocknpu_context* context, const uint8_t* weights, size_t weights_bytes,
+                                  uint32_t quant_kind, size_t k, size_t n) {
+    // L:4074-4121 and prewarm_quantized_m16_with (L:4001-4072): only the
+    // shapes the reference pre-warms; others are a successful no-op.
+    if (!context || !weights || k == 0 || n == 0) return kInvalid;
+    const int kind = quant_kind46(quant_kind);
+    if (!kind || k % 256 != 0) return kInvalid;
+    if (weights_bytes != n * (k / 256) * rk::qblock_bytes(kind)) return kInvalid;
+    const bool shape = (k == 2048 && (n == 256 || n == 2048 || n == 5632)) || (k == 5632 && n == 2048);
+    if (!shape || !mtile_shape_enabled(k, n)) return kOk;
+    if (!bind(context)) return kDeviceError;
+    const Key key = make_key(weights, weights_bytes, k, n, kind);
+    if (context->mtile.count(key)) return kOk;
+    W8Ptr p;
+    Member mb{kind, weights, nullptr, weights_bytes, n};
+    const int st = build_w8(context, &mb, 1, k, p);
+    if (st != kOk) return st;
+    context->mtile.emplace(key, std::move(p));
+    return kOk;
+}
+
+int rocknpu_matmul_f16_f32_f32(rocknpu_context* context, const uint16_t* weights, const float* a, float* out,
+                               size_t m, size_t k, size_t n) {
+    if (!context || !weights || !a || !out || m == 0 || k == 0 || n == 0) return kInvalid;
+    size_t t;
+    if (mul_overflows(m, k, &t) || mul_overflows(n, k, &t) || mul_overflows(m, n, &t)) return kInvalid;
+    if (!bind(context)) return kDeviceError;
+    const Key key = make_key(weights, n * k * 2, k, n, kKindF16);
+    F16Ptr p;
+    auto it = context->f16.find(key);
+    if (it != context->f16.end()) {
+        p = it->second;
+    } else {
+        const int st = build_f16_raw(context, weights, k, n, p);
+        if (st != kOk) return st;
+        context->f16.emplace(key, p);
+    }
+    return run_f16(context, *p, a, m, k, out);
+}
+
+int rocknpu_matmul_w8a8_f32_f32_m1(rocknpu_context* context, const int8_t* weights, const float* scales,
+                                   const float* a, float* out, size_t k, size_t n) {
+    if (!context || !weights || !scales || !a || !out || k == 0 || n == 0) return kInvalid;
+    size_t len;
+    if (mul_overflows(k, n, &len)) return kInvalid;
+    if (!scales_valid(scales, n)) return kInvalid;
+    if (k % 512 != 0 || n % 32 != 0 || n > 8192) return kInvalid;  // L:1578-1585
+    if (!bind(context)) return kDeviceError;
+    const Key key = make_key(weights, len, k, n, kKindW8);
+    Member mb{kKindW8, reinterpret_cast<const uint8_t*>(weights), scales, len, n};
+    OutSeg seg{out, n};
+    return decode_m1(context, KeyList{key}, &mb, 1, a, &seg, k);
+}
+
+int rocknpu_matmul_w8a8_f32_f32_m1_nsplit(rocknpu_context* context, const int8_t* weights, const float* scales,
+                                          const float* a, float* out, size_t k, size_t n, size_t chunk_n) {
+    if (!context || !weights || !scales || !a || !out || k == 0 || n == 0 || chunk_n == 0 || chunk_n % 32 != 0 ||
+        n % 32 != 0)
+        return kInvalid;
+    for (size_t off = 0; off < n;) {
+        const size_t cur = std::min(chunk_n, n - off);
+        const int st = rocknpu_matmul_w8a8_f32_f32_m1(context, weights + off * k, scales + off, a, out + off, k, cur);
+        if (st != kOk) return st;
+        off += cur;
+    }
+    return kOk;
+}
+
+int rocknpu_matmul_w8a8_f32_f32_m16(rocknpu_context* context, const int8_t* weights, const float* scales,
+                                    const float* a, float* out, size_t k, size_t n) {
+    constexpr size_t M = 16;
+    if (!context || !weights || !scales || !a || !out || k == 0 || n == 0) return kInvalid;
+    size_t len;
+    if (mul_overflows(k, n, &len)) return kInvalid;
+    if (!scales_valid(scales, n)) return kInvalid;
+    // execute_cached_w8a8_mtile's checks (L:2818-2827)
+    if (!(k <= 4096 || k == 5632) || k % 512 != 0 || n % 32 != 0 || n > 8192) return kInvalid;
+    if (!bind(context)) return kDeviceError;
+    const Key key = make_key(weights, len, k, n, kKindW8);
+    auto it = context->mtile.find(key);
+    if (it == context->mtile.end()) {
+        W8Ptr p;
+        Member mb{kKindW8, reinterpret_cast<const uint8_t*>(weights), scales, len, n};
+        const int st = build_w8(context, &mb, 1, k, p);
+        if (st != kOk) return st;
+        it = context->mtile.emplace(key, std::move(p)).first;
+    }
+    OutSeg seg{out, n};
+    return run_w8a8(context, *it->second, a, M, k, &seg, 1, false);
+}
+
+int rocknpu_matmul_w8a8_pair_f32_f32_m1(rocknpu_context* context, const int8_t* w1, const float* s1, size_t n1,
+                                        const int8_t* w2, const float* s2, size_t n2, const float* a, float* o1,
+                                        float* o2, size_t k) {
+    if (!context || !w1 || !s1 || !w2 || !s2 || !a || !o1 || !o2 || k == 0 || n1 == 0 || n2 == 0) return kInvalid;
+    size_t l1, l2;
+    if (mul_overflows(k, n1, &l1) || mul_overflows(k, n2, &l2)) return kInvalid;
+    if (!scales_valid(s1, n1) || !scales_valid(s2, n2)) return kInvalid;
+    // execute_cached_w8a8_pair_m1's checks (L:3276-3291)
+    if (k % 512 != 0 || n1 % 32 != 0 || n2 % 32 != 0 || n1 + n2 > 16384) return kInvalid;
+    if (!bind(context)) return kDeviceError;
+    KeyList keys{make_key(w1, l1, k, n1, kKindW8), make_key(w2, l2, k, n2, kKindW8)};
+    Member mb[2] = {{kKindW8, reinterpret_cast<const uint8_t*>(w1), s1, l1, n1},
+                    {kKindW8, reinterpret_cast<const uint8_t*>(w2), s2, l2, n2}};
+    OutSeg segs[2] = {{o1, n1}, {o2, n2}};
+    return decode_m1(context, keys, mb, 2, a, segs, k);
+}
+
+int rocknpu_matmul_w8a8_triple_f32_f32_m1(rocknpu_context* context, const int8_t* w1, const float* s1, size_t n1,
+                                          const int8_t* w2, const float* s2, size_t n2, const int8_t* w3,
+                                          const float* s3, size_t n3, const float* a, float* o1, float* o2,
+                                          float* o3, size_t k) {
+    if (!context || !w1 || !s1 || !w2 || !s2 || !w3 || !s3 || !a || !o1 || !o2 || !o3 || k == 0 || n1 == 0 ||
+        n2 == 0 || n3 == 0)
+        return kInvalid;
+    size_t l1, l2, l3;
+    if (mul_overflows(k, n1, &l1) || mul_overflows(k, n2, &l2) || mul_overflows(k, n3, &l3)) return kInvalid;
+    if (!scales_valid(s1, n1) || !scales_valid(s2, n2) || !scales_valid(s3, n3)) return kInvalid;
+    // execute_cached_w8a8_triple_m1's checks (L:3443-3466)
+    if (k % 512 != 0 || n1 % 32 != 0 || n2 % 32 != 0 || n3 % 32 != 0 || n1 + n2 + n3 > 16384) return kInvalid;
+    if (!bind(context)) return kDeviceError;
+    KeyList keys{make_key(w1, l1, k, n1, kKindW8), make_key(w2, l2, k, n2, kKindW8), make_key(w3, l3, k, n3, kKindW8)};
+    Member mb[3] = {{kKindW8, reinterpret_cast<const uint8_t*>(w1), s1, l1, n1},
+                    {kKindW8, reinterpret_cast<const uint8_t*>(w2), s2, l2, n2},
+                    {kKindW8, reinterpret_cast<const uint8_t*>(w3), s3, l3, n3}};
+    OutSeg segs[3] = {{o1, n1}, {o2, n2}, {o3, n3}};
+    return decode_m1(context, keys, mb, 3, a, segs, k);
+}
+
+int rocknpu_matmul_q_pair_f32_f32_m1(rocknpu_context* context, const uint8_t* w1, size_t b1, uint32_t kind1,
+                                     size_t n1, const uint8_t* w2, size_t b2, uint32_t kind2, size_t n2,
+                                     const float* a, float* o1, float* o2, size_t k) {
+    if (!context || !w1 || !w2 || !a || !o1 || !o2 || k == 0 || n1 == 0 || n2 == 0) return kInvalid;
+    const int k1 = quant_kind46(kind1), k2 = quant_kind46(kind2);
+    if (!k1 || !k2) return kInvalid;
+    if (k % 512 != 0 || n1 % 32 != 0 || n2 % 32 != 0 || n1 + n2 > 16384) return kInvalid;
+    // prepare_q*_k_w8a8's byte check (L:713-717): a mismatch is INVALID
+    if (b1 != n1 * (k / 256) * rk::qblock_bytes(k1) || b2 != n2 * (k / 256) * rk::qblock_bytes(k2)) return kInvalid;
+    if (!bind(context)) return kDeviceError;
+    KeyList keys{make_key(w1, b1, k, n1, k1), make_key(w2, b2, k, n2, k2)};
+    Member mb[2] = {{k1, w1, nullptr, b1, n1}, {k2, w2, nullptr, b2, n2}};
+    OutSeg segs[2] = {{o1, n1}, {o2, n2}};
+    return decode_m1(context, keys, mb, 2, a, segs, k);
+}
+
+int rocknpu_matmul_q_triple_f32_f32_m1(rocknpu_context* context, const uint8_t* w1, size_t b1, uint32_t kind1,
+                                       size_t n1, const uint8_t* w2, size_t b2, uint32_t kind2, size_t n2,
+                                       const uint8_t* w3, size_t b3, uint32_t kind3, size_t n3, const float* a,
+                                       float* o1, float* o2, float* o3, size_t k) {
+    if (!context || !w1 || !w2 || !w3 || !a || !o1 || !o2 || !o3 || k == 0 || n1 == 0 || n2 == 0 || n3 == 0)
+        return kInvalid;
+    const int k1 = quant_kind46(kind1), k2 = quant_kind46(kind2), k3 = quant_kind46(kind3);
+    if (!k1 || !k2 || !k3) return kInvalid;
+    if (k % 512 != 0 || n1 % 32 != 0 || n2 % 32 != 0 || n3 % 32 != 0 || n1 + n2 + n3 > 16384) return kInvalid;
+    if (b1 != n1 * (k / 256) * rk::qblock_bytes(k1) || b2 != n2 * (k / 256) * rk::qblock_bytes(k2) ||
+        b3 != n3 * (k / 256) * rk::qblock_bytes(k3))
+        return kInvalid;
+    if (!bind(context)) return kDeviceError;
+    KeyList keys{make_key(w1, b1, k, n1, k1), make_key(w2, b2, k, n2, k2), make_key(w3, b3, k, n3, k3)};
+    Member mb[3] = {{k1, w1, nullptr, b1, n1}, {k2, w2, nullptr, b2, n2}, {k3, w3, nullptr, b3, n3}};
+    OutSeg segs[3] = {{o1, n1}, {o2, n2}, {o3, n3}};
+    return decode_m1(context, keys, mb, 3, a, segs, k);
+}
+
+int rocknpu_matmul_q_pair_f32_f32_mtile(rocknpu_context* context, const uint8_t* w1, size_t b1, uint32_t kind1,
+                                        size_t n1, const uint8_t* w2, size_t b2, uint32_t kind2, size_t n2,
+                                        const float* a, float* o1, float* o2, size_t m, size_t k) {
+    if (!context || !w1 || !w2 || !a || !o1 || !o2 || m == 0 || k == 0 || n1 == 0 || n2 == 0) return kInvalid;
+    const int k1 = quant_kind46(kind1), k2 = quant_kind46(kind2);
+    if (!k1 || !k2) return kInvalid;
+    // execute_cached_w8a8_mtile_pair_pool's checks (L:2628-2639)
+    if (!mtile_rows(m) || n1 != n2 || k > 4096 || k % 512 != 0 || n1 < 2048 || n1 > 8192 || n1 % 32 != 0)
+        return kInvalid;
+    if (b1 != n1 * (k / 256) * rk::qblock_bytes(k1) || b2 != n2 * (k / 256) * rk::qblock_bytes(k2)) return kInvalid;
+    if (!bind(context)) return kDeviceError;
+    const uint8_t* ws[2] = {w1, w2};
+    const size_t bs[2] = {b1, b2};
+    const int kd[2] = {k1, k2};
+    const size_t ns[2] = {n1, n2};
+    float* outs[2] = {o1, o2};
+    return concat_group(context, 2, ws, bs, kd, ns, a, outs, m, k);
+}
+
+int rocknpu_matmul_w8a8_swiglu_down_f32(rocknpu_context* context, const int8_t* gw, const float* gs,
+                                        const int8_t* uw, const float* us, const int8_t* dw, const float* ds,
+                                        const float* a, float* out, size_t projection_k, size_t ffn_n,
+                                        size_t output_n) {
+    if (!context || !gw || !gs || !uw || !us || !dw || !ds || !a || !out || projection_k == 0 || ffn_n == 0 ||
+        output_n == 0)
+        return kInvalid;
+    size_t t;
+    if (mul_overflows(projection_k, ffn_n, &t) || mul_overflows(ffn_n, output_n, &t)) return kInvalid;
+    std::vector<float> gate(ffn_n), up(ffn_n), act(ffn_n);
+    int st = rocknpu_matmul_w8a8_pair_f32_f32_m1(context, gw, gs, ffn_n, uw, us, ffn_n, a, gate.data(), up.data(),
+                                                 projection_k);
+    if (st != kOk) return st;
+    // f32 SwiGLU on the GPU (L:4368-4373)
+    if (!bind(context)) return kDeviceError;
+    if (context->swiglu_tmp.ensure(3 * ffn_n * sizeof(float))) return kExecError;
+    float* g = context->swiglu_tmp.as<float>();
+    if (cudaMemcpyAsync(g, gate.data(), ffn_n * 4, cudaMemcpyHostToDevice, context->stream) ||
+        cudaMemcpyAsync(g + ffn_n, up.data(), ffn_n * 4, cudaMemcpyHostToDevice, context->stream))
+        return kExecError;
+    rk::launch_swiglu(g, g + ffn_n, g + 2 * ffn_n, static_cast<int>(ffn_n), context->stream);
+    if (cudaGetLastError() ||
+        cudaMemcpyAsync(act.data(), g + 2 * ffn_n, ffn_n * 4, cudaMemcpyDeviceToHost, context->stream) ||
+        cudaStreamSynchronize(context->stream))
+        return kExecError;
+    return rocknpu_matmul_w8a8_f32_f32_m1(context, dw, ds, act.data(), out, ffn_n, output_n);
+}
+
+
+// ---- device-pointer entry points (rocknpu_b200.h) -------------------------
+
+rocknpu_stream rocknpu_b200_context_stream(rocknpu_context* context) {
+    return context ? static_cast<rocknpu_stream>(context->stream) : nullptr;
+}
+
+int rocknpu_b200_context_check(rocknpu_context* context) {
+    if (!context) return kInvalid;
+    if (!bind(context)) return kDeviceError;
+    const int st = finish(context);
+    if (st != kOk) cudaMemset(context->d_status, 0, sizeof(int));
+    return st;
+}
+
+int rocknpu_b200_prepare_w8(uint32_t kind, const uint8_t* blocks, size_t k, size_t n, int8_t* w_i8, float* scales,
+                            int* status, rocknpu_stream stream) {
+    if ((kind != 4 && kind != 5 && kind != 6) || !blocks || !w_i8 || !scales || !status || k == 0 || n == 0 ||
+        k % 256 != 0 || k > 56 * 1024 || n > 0x7fffffff)
+        return kInvalid;
+    rk::launch_prep_w8(static_cast<int>(kind), blocks, static_cast<int>(k), static_cast<int>(n), w_i8, scales, status,
+                       static_cast<cudaStream_t>(stream));
+    return cuda_status(cudaGetLastError());
+}
+
+int rocknpu_b200_quantize_rows(const float* a, size_t m, size_t k, int8_t* a_i8, size_t ld_i8, float* scales,
+                               int* status, rocknpu_stream stream) {
+    if (!a || !a_i8 || !scales || !status || m == 0 || k == 0 || ld_i8 < k || k > 56 * 1024 || m > 0x7fffffff)
+        return kInvalid;
+    rk::launch_quant_rows(a, static_cast<int>(m), static_cast<int>(k), static_cast<long long>(k), a_i8,
+                          static_cast<long long>(ld_i8), scales, status, static_cast<cudaStream_t>(stream));
+    return cuda_status(cudaGetLastError());
+}
+
+int rocknpu_b200_gemm_w8a8(const int8_t* a_i8, size_t ld_a, const float* a_scales, const int8_t* w_i8, size_t ld_w,
+                           const float* w_scales, float* out, size_t ldo, int32_t* acc_out, size_t m, size_t k,
+                           size_t n, int* status, rocknpu_stream stream) {
+    if (!a_i8 || !a_scales || !w_i8 || !w_scales || !out || !status || m == 0 || k == 0 || n == 0 || ld_a < k ||
+        ld_w < k || ldo < n || m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff)
+        return kInvalid;
+    rk::OutMembers om;
+    om.count = 1;
+    om.n_start[1] = static_cast<int>(n);
+    om.out[0] = out;
+    om.ldo[0] = static_cast<long long>(ldo);
+    const int e = rk::launch_gemm_tc(0, w_i8, static_cast<long long>(ld_w), a_i8, static_cast<long long>(ld_a),
+                                     static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), w_scales, a_scales,
+                                     om, acc_out, static_cast<long long>(n), status, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? kOk : (e == cudaErrorInvalidValue ? kInvalid : kExecError);
+}
+
+int rocknpu_b200_matmul_w8a8(rocknpu_context* context, const float* a, const int8_t* w_i8, const float* w_scales,
+                             float* out, size_t m, size_t k, size_t n, rocknpu_stream stream) {
+    if (!context || !a || !w_i8 || !w_scales || !out || m == 0 || k == 0 || n == 0) return kInvalid;
+    if (!bind(context)) return kDeviceError;
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : context->stream;
+    const size_t ld8 = round_up(k, 16);
+    if (context->a_i8.ensure(m * ld8) || context->a_scale.ensure(m * sizeof(float))) return kExecError;
+    rk::launch_quant_rows(a, static_cast<int>(m), static_cast<int>(k), static_cast<long long>(k),
+                          context->a_i8.as<int8_t>(), static_cast<long long>(ld8), context->a_scale.as<float>(),
+                          context->d_status, s);
+    if (m == 1 && k % 16 == 0) {
+        rk::launch_gemv_w8a8(w_i8, w_scales, context->a_i8.as<int8_t>(), context->a_scale.as<float>(),
+                             static_cast<int>(k), static_cast<int>(n), out, s);
+        return cuda_status(cudaGetLastError());
+    }
+    return rocknpu_b200_gemm_w8a8(context->a_i8.as<int8_t>(), ld8, context->a_scale.as<float>(), w_i8, k, w_scales,
+                                  out, n, nullptr, m, k, n, context->d_status, s);
+}
+
+int rocknpu_b200_gemm_f16(const uint16_t* a_f16, size_t ld_a, const uint16_t* w_f16, size_t ld_w, float* out,
+                          size_t ldo, size_t m, size_t k, size_t n, int* status, rocknpu_stream stream) {
+    if (!a_f16 || !w_f16 || !out || !status || m == 0 || k == 0 || n == 0 || ld_a < k || ld_w < k || ldo < n ||
+        m > 0x7fffffff || n > 0x7fffffff)
+        return kInvalid;
+    rk::OutMembers om;
+    om.count = 1;
+    om.n_start[1] = static_cast<int>(n);
+    om.out[0] = out;
+    om.ldo[0] = static_cast<long long>(ldo);
+    const int e = rk::launch_gemm_tc(1, w_f16, static_cast<long long>(ld_w * 2), a_f16,
+                                     static_cast<long long>(ld_a * 2), static_cast<int>(m), static_cast<int>(n),
+                                     static_cast<int>(k), nullptr, nullptr, om, nullptr, 0, status,
+                                     static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? kOk : (e == cudaErrorInvalidValue ? kInvalid : kExecError);
+}
+
+int rocknpu_b200_gemv_w8a8(const int8_t* a_i8, const float* a_scale, const int8_t* w_i8, const float* w_scales,
+                           float* out, size_t k, size_t n, rocknpu_stream stream) {
+    if (!a_i8 || !a_scale || !w_i8 || !w_scales || !out || k == 0 || n == 0 || k % 16 != 0 || k > 200 * 1024 ||
+        n > 0x7fffffff)
+        return kInvalid;
+    rk::launch_gemv_w8a8(w_i8, w_scales, a_i8, a_scale, static_cast<int>(k), static_cast<int>(n), out,
+                         static_cast<cudaStream_t>(stream));
+    return cuda_status(cudaGetLastError());
+}
+
+}  // extern "C"

@@ -1,0 +1,69 @@
+// K5: M=1 W8A8 GEMV for decode (execute_cached_w8a8_m1,
+// capi/src/lib.rs:1567-1701), HBM-bound on the resident int8 weights.
+//
+// One warp per output row: the quantised activation (K bytes) is staged once
+// per CTA in shared memory; each lane streams 16-byte weight chunks with
+// no-L1-allocate loads, four dp4a per chunk, an exact int32 warp sum, and
+// lane 0 applies the reference's rescale (f32(acc) * a_scale) * w_scale.
+#include "kernels.h"
+
+namespace rk {
+namespace {
+
+constexpr int kGemvThreads = 256;
+constexpr int kRowsPerCta = kGemvThreads / 32;
+
+__device__ __forceinline__ int4 ld_stream(const int4* p) {
+    int4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__global__ void __launch_bounds__(kGemvThreads) gemv_w8a8_kernel(const int8_t* __restrict__ w,
+                                                                  const float* __restrict__ w_scale,
+                                                                  const int8_t* __restrict__ a8,
+                                                                  const float* __restrict__ a_scale, int k, int n,
+                                                                  float* __restrict__ out) {
+    extern __shared__ int4 sa[];
+    const int chunks = k >> 4;
+    for (int i = threadIdx.x; i < chunks; i += kGemvThreads) sa[i] = reinterpret_cast<const int4*>(a8)[i];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = blockIdx.x * kRowsPerCta + warp;
+    if (row >= n) return;
+    const int4* wr = reinterpret_cast<const int4*>(w + static_cast<size_t>(row) * k);
+    int acc = 0;
+    int i = lane;
+    for (; i + 96 < chunks; i += 128) {
+        const int4 w0 = ld_stream(wr + i), w1 = ld_stream(wr + i + 32), w2 = ld_stream(wr + i + 64),
+                   w3 = ld_stream(wr + i + 96);
+        const int4 a0 = sa[i], a1 = sa[i + 32], a2 = sa[i + 64], a3 = sa[i + 96];
+        acc = __dp4a(w0.x, a0.x, acc); acc = __dp4a(w0.y, a0.y, acc); acc = __dp4a(w0.z, a0.z, acc); acc = __dp4a(w0.w, a0.w, acc);
+        acc = __dp4a(w1.x, a1.x, acc); acc = __dp4a(w1.y, a1.y, acc); acc = __dp4a(w1.z, a1.z, acc); acc = __dp4a(w1.w, a1.w, acc);
+        acc = __dp4a(w2.x, a2.x, acc); acc = __dp4a(w2.y, a2.y, acc); acc = __dp4a(w2.z, a2.z, acc); acc = __dp4a(w2.w, a2.w, acc);
+        acc = __dp4a(w3.x, a3.x, acc); acc = __dp4a(w3.y, a3.y, acc); acc = __dp4a(w3.z, a3.z, acc); acc = __dp4a(w3.w, a3.w, acc);
+    }
+    for (; i < chunks; i += 32) {
+        const int4 w0 = ld_stream(wr + i);
+        const int4 a0 = sa[i];
+        acc = __dp4a(w0.x, a0.x, acc); acc = __dp4a(w0.y, a0.y, acc); acc = __dp4a(w0.z, a0.z, acc); acc = __dp4a(w0.w, a0.w, acc);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) out[row] = __fmul_rn(__fmul_rn(__int2float_rn(acc), *a_scale), w_scale[row]);
+}
+
+}  // namespace
+
+void launch_gemv_w8a8(const int8_t* w, const float* w_scale, const int8_t* a8, const float* a_scale, int k, int n,
+                      float* out, cudaStream_t s) {
+    const size_t smem = static_cast<size_t>(k);
+    if (smem > 48 * 1024)
+        cudaFuncSetAttribute(gemv_w8a8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    gemv_w8a8_kernel<<<(n + kRowsPerCta - 1) / kRowsPerCta, kGemvThreads, smem, s>>>(w, w_scale, a8, a_scale, k, n,
+                                                                                     out);
+}
+
+}  // namespace rk

@@ -1,0 +1,57 @@
+// Host-side launchers of the sm_100a kernels (device pointers, one stream).
+// The C ABI in capi.cpp is the only caller inside the library.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace rk {
+
+enum QKind : int { kQ4K = 4, kQ5K = 5, kQ6K = 6 };
+
+inline size_t qblock_bytes(int kind) {
+    return kind == kQ4K ? 144 : kind == kQ5K ? 176 : kind == kQ6K ? 210 : 0;
+}
+
+// Up to four output members of one concatenated-N GEMM: member i owns the
+// weight rows [n_start[i], n_start[i+1]) and writes out[i][m * ldo[i] + col].
+struct OutMembers {
+    int count = 1;
+    int n_start[5] = {0, 0, 0, 0, 0};
+    float* out[4] = {nullptr, nullptr, nullptr, nullptr};
+    long long ldo[4] = {0, 0, 0, 0};
+};
+
+// K1: Q4_K/Q5_K/Q6_K rows -> int8 rows [n, k] + per-row scales [n].
+void launch_prep_w8(int kind, const uint8_t* blocks, int k, int n, int8_t* w, float* scales, int* err,
+                    cudaStream_t s);
+// K1 (FP16 route): Q rows -> f16 rows [n, ldw] (dequantised, rounded to f16).
+void launch_dequant_f16(int kind, const uint8_t* blocks, int k, int n, __half* w, long long ldw, int* err,
+                        cudaStream_t s);
+// K2: per-token symmetric int8 [m, ld8] + scales [m]; non-finite -> *err.
+void launch_quant_rows(const float* a, int m, int k, long long lda, int8_t* a8, long long ld8, float* scales,
+                       int* err, cudaStream_t s);
+// FP16 executor input: f32 [m, k] -> f16 [m, ldo] (round to nearest even).
+void launch_f32_to_f16(const float* a, int m, int k, long long lda, __half* out, long long ldo, cudaStream_t s);
+
+// K3/K4: out = epilogue(W[n,k] . A[m,k]^T) on tcgen05.  kind 0: int8 inputs,
+// int32 accumulators, out = (f32(acc) * a_scale[m]) * w_scale[n]; kind 1:
+// f16 inputs, f32 accumulators, out = acc.  ld*_bytes are row pitches
+// (multiples of 16).  acc_out (kind 0, optional) receives the raw int32.
+// Returns a cudaError_t value.
+int launch_gemm_tc(int kind, const void* w, long long ldw_bytes, const void* a, long long lda_bytes, int m, int n,
+                   int k, const float* w_scale, const float* a_scale, const OutMembers& outs, int32_t* acc_out,
+                   long long acc_ld, int* err, cudaStream_t s);
+
+// K5: M=1 W8A8 GEMV over resident int8 rows.
+void launch_gemv_w8a8(const int8_t* w, const float* w_scale, const int8_t* a8, const float* a_scale, int k, int n,
+                      float* out, cudaStream_t s);
+
+// SwiGLU between the M=1 gate/up and down projections.
+void launch_swiglu(const float* gate, const float* up, float* out, int n, cudaStream_t s);
+
+int sm_count();
+
+}  // namespace rk

@@ -1,0 +1,302 @@
+// K1 (weight preparation) and K2 (per-token activation quantisation).
+//
+// Both are HBM-bound byte/float streams: one CTA per row, coalesced vector
+// loads, the dequantised (or loaded) row staged once in shared memory, a
+// block-wide absmax, then 16-byte int8 stores.  Arithmetic follows the
+// reference exactly (no contraction, IEEE division, round half away from
+// zero), so the int8 values are bit-identical to its CPU path.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace rk {
+namespace {
+
+constexpr int kRowThreads = 256;
+
+__device__ __forceinline__ uint32_t ld32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+__device__ __forceinline__ uint32_t ld16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
+
+__device__ __forceinline__ float half_bits_to_float(uint32_t bits) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(bits & 0xFFFFu)));
+}
+
+// 6-bit scale/min pair j of a Q4_K/Q5_K superblock; s[] holds its 12 bytes.
+__device__ __forceinline__ void scale_min_k4(int j, const uint8_t* s, int& sc, int& m) {
+    if (j < 4) {
+        sc = s[j] & 63;
+        m = s[j + 4] & 63;
+    } else {
+        sc = (s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4);
+        m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+}
+
+// Dequantise the 8 values that thread `l` (0..31) owns in one superblock and
+// hand them to `put(index_in_block, value)`.  Value formulas follow the
+// llama-gguf dequantisers the reference calls (capi/src/lib.rs:732-733,
+// 986-988): Q4_K/Q5_K (d*sc)*q - (dmin*m), Q6_K (d*sc)*(q-32), f32 each step.
+template <int KIND, class Put>
+__device__ __forceinline__ void dequant8(const uint8_t* blk, int l, Put&& put) {
+    if constexpr (KIND == kQ4K || KIND == kQ5K) {
+        const uint32_t dd = ld32(blk);
+        const float d = half_bits_to_float(dd), dmin = half_bits_to_float(dd >> 16);
+        uint8_t s[12];
+        *reinterpret_cast<uint32_t*>(s) = ld32(blk + 4);
+        *reinterpret_cast<uint32_t*>(s + 4) = ld32(blk + 8);
+        *reinterpret_cast<uint32_t*>(s + 8) = ld32(blk + 12);
+        const int g = l >> 3, i4 = (l & 7) * 4;
+        int sc, mn;
+        scale_min_k4(2 * g, s, sc, mn);
+        const float d1 = __fmul_rn(d, static_cast<float>(sc)), m1 = __fmul_rn(dmin, static_cast<float>(mn));
+        scale_min_k4(2 * g + 1, s, sc, mn);
+        const float d2 = __fmul_rn(d, static_cast<float>(sc)), m2 = __fmul_rn(dmin, static_cast<float>(mn));
+        const uint32_t q = ld32(blk + (KIND == kQ4K ? 16 : 48) + 32 * g + i4);
+        uint32_t h = 0;
+        if constexpr (KIND == kQ5K) h = ld32(blk + 16 + i4);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            int lo = (q >> (8 * i)) & 0x0F, hi = (q >> (8 * i + 4)) & 0x0F;
+            if constexpr (KIND == kQ5K) {
+                const uint32_t hb = (h >> (8 * i)) & 0xFF;
+                lo |= ((hb >> (2 * g)) & 1) << 4;
+                hi |= ((hb >> (2 * g + 1)) & 1) << 4;
+            }
+            put(64 * g + i4 + i, __fsub_rn(__fmul_rn(d1, static_cast<float>(lo)), m1));
+            put(64 * g + 32 + i4 + i, __fsub_rn(__fmul_rn(d2, static_cast<float>(hi)), m2));
+        }
+    } else {
+        const float d = half_bits_to_float(ld16(blk + 208));
+        const int h = l >> 4, lp = (l & 15) * 2;
+        const uint32_t qa = ld16(blk + 64 * h + lp);
+        const uint32_t qb = ld16(blk + 64 * h + 32 + lp);
+        const uint32_t qh = ld16(blk + 128 + 32 * h + lp);
+        const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192);
+        float ds[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) ds[t] = __fmul_rn(d, static_cast<float>(sc[8 * h + 2 * t + (lp >> 4)]));
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const uint32_t a = (qa >> (8 * e)) & 0xFF, b = (qb >> (8 * e)) & 0xFF, hb = (qh >> (8 * e)) & 0xFF;
+            const int q0 = static_cast<int>((a & 0x0F) | ((hb & 3) << 4)) - 32;
+            const int q1 = static_cast<int>((b & 0x0F) | (((hb >> 2) & 3) << 4)) - 32;
+            const int q2 = static_cast<int>((a >> 4) | (((hb >> 4) & 3) << 4)) - 32;
+            const int q3 = static_cast<int>((b >> 4) | (((hb >> 6) & 3) << 4)) - 32;
+            const int base = 128 * h + lp + e;
+            put(base, __fmul_rn(ds[0], static_cast<float>(q0)));
+            put(base + 32, __fmul_rn(ds[1], static_cast<float>(q1)));
+            put(base + 64, __fmul_rn(ds[2], static_cast<float>(q2)));
+            put(base + 96, __fmul_rn(ds[3], static_cast<float>(q3)));
+        }
+    }
+}
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int warp = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) red[warp] = v;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float w = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) w = fmaxf(w, __shfl_xor_sync(0xffffffffu, w, o));
+        if (threadIdx.x == 0) red[32] = w;
+    }
+    __syncthreads();
+    return red[32];
+}
+
+// quantize_symmetric_into's per-value step (capi/src/lib.rs:650-652):
+// round_half_away(x / scale) clamped to +-127.
+__device__ __forceinline__ int quant_value(float x, float scale) {
+    float q = roundf(__fdiv_rn(x, scale));
+    q = fminf(fmaxf(q, -127.0f), 127.0f);
+    return static_cast<int>(q);
+}
+
+// Quantise a shared-memory row of k floats (k % 16 == 0) to int8 `dst`.
+__device__ __forceinline__ void quantize_smem_row(const float* row, int k, float scale, int8_t* dst) {
+    for (int i = threadIdx.x * 16; i < k; i += blockDim.x * 16) {
+        uint32_t packed[4];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const float4 v = *reinterpret_cast<const float4*>(row + i + 4 * w);
+            packed[w] = (quant_value(v.x, scale) & 0xFF) | ((quant_value(v.y, scale) & 0xFF) << 8) |
+                        ((quant_value(v.z, scale) & 0xFF) << 16) | ((quant_value(v.w, scale) & 0xFF) << 24);
+        }
+        *reinterpret_cast<uint4*>(dst + i) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    }
+}
+
+// K1: one CTA per weight row (prepare_q*_k_w8a8, capi/src/lib.rs:711-757,
+// 974-994): dequantise into shared memory, absmax, int8 + scale.
+template <int KIND>
+__global__ void __launch_bounds__(kRowThreads) prep_w8_kernel(const uint8_t* __restrict__ blocks, int k,
+                                                               int8_t* __restrict__ w, float* __restrict__ scales,
+                                                               int* __restrict__ err) {
+    extern __shared__ __align__(16) float srow[];
+    __shared__ float red[33];
+    const int row = blockIdx.x;
+    const int nb = k >> 8;
+    const size_t bb = KIND == kQ4K ? 144 : KIND == kQ5K ? 176 : 210;
+    const uint8_t* src = blocks + static_cast<size_t>(row) * nb * bb;
+    float amax = 0.0f;
+    bool finite = true;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int b = warp; b < nb; b += kRowThreads / 32) {
+        float* dst = srow + b * 256;
+        dequant8<KIND>(src + b * bb, lane, [&](int idx, float v) {
+            dst[idx] = v;
+            finite &= isfinite(v);
+            amax = fmaxf(amax, fabsf(v));
+        });
+    }
+    if (__syncthreads_or(!finite)) {
+        if (threadIdx.x == 0) atomicExch(err, kErrNonFinite);
+        return;
+    }
+    const float mx = block_max(amax, red);
+    const float scale = mx == 0.0f ? 1.0f : __fdiv_rn(mx, 127.0f);
+    quantize_smem_row(srow, k, scale, w + static_cast<size_t>(row) * k);
+    if (threadIdx.x == 0) scales[row] = scale;
+}
+
+// FP16 route (dequantize_q*_k_prefill_f16, capi/src/lib.rs:393-455):
+// dequantise and round each value to f16; no finiteness check.
+template <int KIND>
+__global__ void __launch_bounds__(kRowThreads) dequant_f16_kernel(const uint8_t* __restrict__ blocks, int k,
+                                                                   __half* __restrict__ w, long long ldw) {
+    const int row = blockIdx.x;
+    const int nb = k >> 8;
+    const size_t bb = KIND == kQ4K ? 144 : KIND == kQ5K ? 176 : 210;
+    const uint8_t* src = blocks + static_cast<size_t>(row) * nb * bb;
+    __half* out = w + static_cast<size_t>(row) * ldw;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int b = warp; b < nb; b += kRowThreads / 32) {
+        __half* dst = out + b * 256;
+        dequant8<KIND>(src + b * bb, lane, [&](int idx, float v) { dst[idx] = __float2half_rn(v); });
+    }
+}
+
+// K2: per-token quantisation (quantize_symmetric_into over each activation
+// row, capi/src/lib.rs:1776-1791).  Rows whose length is not a multiple of 16
+// are zero-padded in shared memory; the padding quantises to 0.
+__global__ void __launch_bounds__(kRowThreads) quant_rows_kernel(const float* __restrict__ a, int k, long long lda,
+                                                                  int8_t* __restrict__ a8, long long ld8,
+                                                                  float* __restrict__ scales,
+                                                                  int* __restrict__ err) {
+    extern __shared__ __align__(16) float srow[];
+    __shared__ float red[33];
+    const int row = blockIdx.x;
+    const float* src = a + static_cast<size_t>(row) * lda;
+    const int k16 = (k + 15) & ~15;
+    float amax = 0.0f;
+    bool finite = true;
+    const bool vec = ((reinterpret_cast<uintptr_t>(src) & 15) == 0) && (k % 4 == 0);
+    if (vec) {
+        for (int i = threadIdx.x * 4; i < k; i += kRowThreads * 4) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(src + i));
+            *reinterpret_cast<float4*>(srow + i) = v;
+            finite &= isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w);
+            amax = fmaxf(fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y))), fmaxf(fabsf(v.z), fabsf(v.w)));
+        }
+    } else {
+        for (int i = threadIdx.x; i < k; i += kRowThreads) {
+            const float v = src[i];
+            srow[i] = v;
+            finite &= isfinite(v);
+            amax = fmaxf(amax, fabsf(v));
+        }
+    }
+    for (int i = k + threadIdx.x; i < k16; i += kRowThreads) srow[i] = 0.0f;
+    if (__syncthreads_or(!finite)) {
+        if (threadIdx.x == 0) atomicExch(err, kErrNonFinite);
+        return;
+    }
+    const float mx = block_max(amax, red);
+    const float scale = mx == 0.0f ? 1.0f : __fdiv_rn(mx, 127.0f);
+    int8_t* dst = a8 + static_cast<size_t>(row) * ld8;
+    if ((ld8 % 16) == 0 && (reinterpret_cast<uintptr_t>(a8) & 15) == 0 && k16 <= ld8) {
+        quantize_smem_row(srow, k16, scale, dst);
+    } else {
+        for (int i = threadIdx.x; i < k; i += kRowThreads) dst[i] = static_cast<int8_t>(quant_value(srow[i], scale));
+    }
+    if (threadIdx.x == 0) scales[row] = scale;
+}
+
+__global__ void f32_to_f16_kernel(const float* __restrict__ a, int m, int k, long long lda, __half* __restrict__ out,
+                                  long long ldo) {
+    const long long total = static_cast<long long>(m) * k;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long r = i / k, c = i % k;
+        out[r * ldo + c] = __float2half_rn(a[r * lda + c]);
+    }
+}
+
+// F32 SwiGLU (capi/src/lib.rs:4368-4373): g * (1 / (1 + exp(-g))) * u.
+__global__ void swiglu_kernel(const float* __restrict__ gate, const float* __restrict__ up, float* __restrict__ out,
+                              int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) {
+        const float g = gate[i];
+        const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
+        out[i] = __fmul_rn(__fmul_rn(g, sig), up[i]);
+    }
+}
+
+template <class F>
+void set_smem(F* f, size_t bytes) {
+    // dynamic + static shared memory above 48 KB needs the opt-in
+    if (bytes > 40 * 1024) cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+}
+
+}  // namespace
+
+void launch_prep_w8(int kind, const uint8_t* blocks, int k, int n, int8_t* w, float* scales, int* err,
+                    cudaStream_t s) {
+    const size_t smem = static_cast<size_t>(k) * sizeof(float);
+    if (kind == kQ4K) {
+        set_smem(prep_w8_kernel<kQ4K>, smem);
+        prep_w8_kernel<kQ4K><<<n, kRowThreads, smem, s>>>(blocks, k, w, scales, err);
+    } else if (kind == kQ5K) {
+        set_smem(prep_w8_kernel<kQ5K>, smem);
+        prep_w8_kernel<kQ5K><<<n, kRowThreads, smem, s>>>(blocks, k, w, scales, err);
+    } else {
+        set_smem(prep_w8_kernel<kQ6K>, smem);
+        prep_w8_kernel<kQ6K><<<n, kRowThreads, smem, s>>>(blocks, k, w, scales, err);
+    }
+}
+
+void launch_dequant_f16(int kind, const uint8_t* blocks, int k, int n, __half* w, long long ldw, int* /*err*/,
+                        cudaStream_t s) {
+    if (kind == kQ4K)
+        dequant_f16_kernel<kQ4K><<<n, kRowThreads, 0, s>>>(blocks, k, w, ldw);
+    else if (kind == kQ5K)
+        dequant_f16_kernel<kQ5K><<<n, kRowThreads, 0, s>>>(blocks, k, w, ldw);
+    else
+        dequant_f16_kernel<kQ6K><<<n, kRowThreads, 0, s>>>(blocks, k, w, ldw);
+}
+
+void launch_quant_rows(const float* a, int m, int k, long long lda, int8_t* a8, long long ld8, float* scales,
+                       int* err, cudaStream_t s) {
+    const size_t smem = static_cast<size_t>((k + 15) & ~15) * sizeof(float);
+    set_smem(quant_rows_kernel, smem);
+    quant_rows_kernel<<<m, kRowThreads, smem, s>>>(a, k, lda, a8, ld8, scales, err);
+}
+
+void launch_f32_to_f16(const float* a, int m, int k, long long lda, __half* out, long long ldo, cudaStream_t s) {
+    const long long total = static_cast<long long>(m) * k;
+    const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+    f32_to_f16_kernel<<<blocks, 256, 0, s>>>(a, m, k, lda, out, ldo);
+}
+
+void launch_swiglu(const float* gate, const float* up, float* out, int n, cudaStream_t s) {
+    swiglu_kernel<<<(n + 255) / 256, 256, 0, s>>>(gate, up, out, n);
+}
+
+}  // namespace rk

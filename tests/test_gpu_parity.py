@@ -1,0 +1,304 @@
+"""GPU parity: the sm_100a kernels and the C ABI against the CPU oracle.
+
+Bit-exact for int8 weights/activations, int32 accumulators and (because the
+rescale is evaluated in the reference's order with the same IEEE operations)
+the f32 W8A8 outputs; the FP16 executor within rtol 1e-3 of the f64 oracle.
+"""
+import numpy as np
+import pytest
+
+import oracle
+import rocknpu_b200 as rk
+from conftest import random_kquant_blocks
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+def _bits(a):
+    return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+
+
+@pytest.fixture(scope="module")
+def dev():
+    from rocknpu_b200 import device
+    return device
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    rk.apply_default_env()
+    c = rk.Context()
+    yield c
+    c.close()
+
+
+# ---- K1: weight preparation ---------------------------------------------------
+
+@pytest.mark.parametrize("kind", [4, 5, 6])
+@pytest.mark.parametrize("k,n", [(256, 8), (2048, 64), (5632, 33), (12288, 4)])
+def test_prepare_w8_bit_exact(dev, rng, kind, k, n):
+    blocks = random_kquant_blocks(kind, n * k // 256, rng)
+    st, w_ref, s_ref = oracle.prepare_w8a8(kind, blocks, k, n)
+    assert st == 0
+    status = dev.new_status()
+    w, s = dev.prepare_w8(kind, torch.from_numpy(blocks).cuda(), k, n, status)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    assert np.array_equal(w.cpu().numpy(), w_ref)
+    assert np.array_equal(_bits(s.cpu().numpy()), _bits(s_ref))
+
+
+def test_prepare_golden_sidecar(dev):
+    import os
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "w8_sidecar.npz"))
+    for kind in (4, 5, 6):
+        n, k = (int(v) for v in g[f"q{kind}_shape"])
+        status = dev.new_status()
+        w, s = dev.prepare_w8(kind, torch.from_numpy(g[f"q{kind}_blocks"]).cuda(), k, n, status)
+        torch.cuda.synchronize()
+        assert status.item() == 0
+        assert np.array_equal(w.cpu().numpy(), g[f"q{kind}_w8"])
+        assert np.array_equal(_bits(s.cpu().numpy()), _bits(g[f"q{kind}_scale"]))
+
+
+def test_prepare_flags_non_finite(dev):
+    blk = np.zeros(144, dtype=np.uint8)
+    blk[0:2] = np.array([np.inf], dtype=np.float16).view(np.uint8)
+    blk[4] = 1
+    status = dev.new_status()
+    dev.prepare_w8(4, torch.from_numpy(blk).cuda(), 256, 1, status)
+    torch.cuda.synchronize()
+    assert status.item() == 1
+
+
+# ---- K2: activation quantisation ----------------------------------------------
+
+@pytest.mark.parametrize("m,k", [(1, 2048), (7, 512), (128, 2048), (33, 5632), (3, 8192), (2, 100)])
+def test_quantize_rows_bit_exact(dev, rng, m, k):
+    a = (rng.standard_normal((m, k)) * rng.uniform(0.01, 50, size=(m, 1))).astype(np.float32)
+    if m > 2:
+        a[1] = 0.0
+    st, q_ref, s_ref = oracle.quantize_rows(a)
+    status = dev.new_status()
+    q, s = dev.quantize_rows(torch.from_numpy(a).cuda(), status)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+    assert np.array_equal(_bits(s.cpu().numpy()), _bits(s_ref))
+
+
+def test_quantize_tie_vector(dev):
+    import os
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "act_quant.npz"))
+    v = g["ties"]
+    v = np.concatenate([v, np.zeros((-v.size) % 16, dtype=np.float32)]).reshape(1, -1)
+    status = dev.new_status()
+    q, s = dev.quantize_rows(torch.from_numpy(v).cuda(), status)
+    torch.cuda.synchronize()
+    assert np.array_equal(q.cpu().numpy()[0, :g["ties"].size], g["ties_q"])
+    assert _bits(s.cpu().numpy())[0] == _bits(g["ties_scale"])[0]
+
+
+def test_quantize_flags_non_finite(dev):
+    a = np.ones((4, 256), dtype=np.float32)
+    a[2, 100] = np.nan
+    status = dev.new_status()
+    dev.quantize_rows(torch.from_numpy(a).cuda(), status)
+    torch.cuda.synchronize()
+    assert status.item() == 1
+
+
+# ---- K3: W8A8 GEMM (int32 exact) ------------------------------------------------
+
+GEMM_SHAPES = [
+    (128, 2048, 5632),
+    (1, 512, 128), (5, 256, 96), (16, 2048, 256), (17, 1024, 200), (64, 768, 384),
+    (100, 4096, 128), (129, 512, 160), (300, 1024, 640), (512, 2048, 2560), (256, 5632, 2048),
+]
+
+
+@pytest.mark.parametrize("m,k,n", GEMM_SHAPES)
+def test_gemm_w8a8_int32_exact(dev, rng, m, k, n):
+    a8 = rng.integers(-127, 128, size=(m, k), dtype=np.int8)
+    w8 = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
+    a_s = rng.uniform(0.001, 0.1, size=m).astype(np.float32)
+    w_s = rng.uniform(0.001, 0.1, size=n).astype(np.float32)
+    acc_ref = oracle.gemm_i8_i32(a8, w8)
+    status = dev.new_status()
+    acc = torch.empty((m, n), dtype=torch.int32, device="cuda")
+    out = dev.gemm_w8a8(torch.from_numpy(a8).cuda(), torch.from_numpy(a_s).cuda(), torch.from_numpy(w8).cuda(),
+                        torch.from_numpy(w_s).cuda(), status, acc=acc)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    assert np.array_equal(acc.cpu().numpy(), acc_ref)
+    exp = np.empty((m, n), dtype=np.float32)
+    for r in range(m):
+        oracle.lib().orc_rescale_i32_row(oracle._p(np.ascontiguousarray(acc_ref[r])), oracle._p(w_s),
+                                         float(a_s[r]), oracle._p(exp[r]), n)
+    assert np.array_equal(_bits(out.cpu().numpy()), _bits(exp))
+
+
+@pytest.mark.parametrize("m", [4, 8, 12, 16, 32, 48, 64, 128])
+def test_gemm_mtile_kat(dev, m):
+    # crates/rocket-smoke/src/bin/int8_mtile.rs:28-86
+    K, N = 2048, 2048
+    a8 = np.repeat(((np.arange(m) % 5) + 1).astype(np.int8)[:, None], K, axis=1)
+    w8 = np.ones((N, K), dtype=np.int8)
+    status = dev.new_status()
+    acc = torch.empty((m, N), dtype=torch.int32, device="cuda")
+    dev.gemm_w8a8(torch.from_numpy(a8).cuda(), torch.ones(m, device="cuda"), torch.from_numpy(w8).cuda(),
+                  torch.ones(N, device="cuda"), status, acc=acc)
+    torch.cuda.synchronize()
+    assert np.all(acc.cpu().numpy() == (K * ((np.arange(m) % 5) + 1))[:, None])
+
+
+def test_gemm_ksplit_kat(dev):
+    # crates/rocket-smoke/src/bin/int8_mtile_ksplit.rs:20-33
+    M, K, n = 16, 5632, 2048
+    r, kk = np.meshgrid(np.arange(M), np.arange(K), indexing="ij")
+    a8 = (((r * 7 + kk * 3 + 5) % 13) - 6).astype(np.int8)
+    c_, kk2 = np.meshgrid(np.arange(n), np.arange(K), indexing="ij")
+    w8 = (((c_ * 5 + kk2 * 11 + 3) % 17) - 8).astype(np.int8)
+    status = dev.new_status()
+    acc = torch.empty((M, n), dtype=torch.int32, device="cuda")
+    dev.gemm_w8a8(torch.from_numpy(a8).cuda(), torch.ones(M, device="cuda"), torch.from_numpy(w8).cuda(),
+                  torch.ones(n, device="cuda"), status, acc=acc)
+    torch.cuda.synchronize()
+    assert np.array_equal(acc.cpu().numpy(), oracle.gemm_i8_i32(a8, w8))
+
+
+# ---- K5: M=1 GEMV ---------------------------------------------------------------
+
+def test_gemv_decode_m1_kat(dev):
+    # crates/rocket-smoke/src/bin/int8_decode_m1.rs:35-45
+    k, n = 2048, 2048
+    a8 = (((np.arange(k) * 7 + 3) % 9) - 4).astype(np.int8)
+    w8 = (((np.arange(n * k) * 5 + 1) % 11) - 5).astype(np.int8).reshape(n, k)
+    out = dev.gemv_w8a8(torch.from_numpy(a8).cuda(), torch.ones(1, device="cuda"), torch.from_numpy(w8).cuda(),
+                        torch.ones(n, device="cuda"))
+    torch.cuda.synchronize()
+    ref = (w8.astype(np.int64) @ a8.astype(np.int64)).astype(np.float32)
+    assert np.array_equal(out.cpu().numpy(), ref)
+
+
+# ---- C ABI end to end --------------------------------------------------------------
+
+@pytest.mark.parametrize("kind", [4, 6])
+@pytest.mark.parametrize("m,k,n", [(128, 2048, 5632), (1, 2048, 256), (5, 512, 64), (16, 2048, 2048),
+                                   (300, 2048, 96), (77, 5632, 256), (8, 2304, 128)])
+def test_capi_matmul_q_bit_exact(ctx, rng, kind, m, k, n):
+    blocks = rk.synth_q_weights(kind, n, k, seed=11 + m)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    out = np.full((m, n), np.nan, dtype=np.float32)
+    assert ctx.matmul_q(kind, blocks, a, out, m, k, n) == 0
+    st, ref = oracle.matmul_q(kind, blocks, a, n)
+    assert st == 0
+    assert np.array_equal(_bits(out), _bits(ref))
+    # second call hits the resident weight cache
+    out2 = np.zeros_like(out)
+    assert ctx.matmul_q(kind, blocks, a, out2, m, k, n) == 0
+    assert np.array_equal(_bits(out2), _bits(ref))
+
+
+def test_capi_q5_prompt(ctx, rng):
+    m, k, n = 32, 1024, 96
+    blocks = rk.synth_q_weights(5, n, k, seed=5)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    out = np.empty((m, n), dtype=np.float32)
+    assert ctx.matmul_q(5, blocks, a, out, m, k, n) == 0
+    st, ref = oracle.matmul_q(5, blocks, a, n)
+    assert np.array_equal(_bits(out), _bits(ref))
+    assert ctx.matmul_q(5, blocks, a[:1], out[:1], 1, k, n) == -1  # Q5_K has no M=1 route
+
+
+def test_capi_fp16_route_for_unaligned_n(ctx, rng):
+    # n % 32 != 0: no W8A8 branch accepts it, the FP16 route runs
+    m, k, n = 8, 512, 48
+    blocks = rk.synth_q_weights(4, n, k, seed=3)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    out = np.empty((m, n), dtype=np.float32)
+    assert ctx.matmul_q(4, blocks, a, out, m, k, n) == 0
+    w16 = oracle.dequant(4, blocks).astype(np.float16).reshape(n, k)
+    ref = oracle.matmul_f16(w16.view(np.uint16), a)
+    np.testing.assert_allclose(out, ref, rtol=1e-3, atol=1e-3 * np.abs(ref).max())
+
+
+def test_capi_rejects_non_finite(ctx, rng):
+    m, k, n = 4, 512, 64
+    blocks = rk.synth_q_weights(4, n, k, seed=4)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    a[2, 3] = np.inf
+    out = np.zeros((m, n), dtype=np.float32)
+    assert ctx.matmul_q(4, blocks, a, out, m, k, n) == -1
+    assert not out.any()  # output untouched on error
+    a[2, 3] = 0.0
+    assert ctx.matmul_q(4, blocks, a, out, m, k, n) == 0  # context still usable
+
+
+def test_capi_rejects_bad_sizes(ctx, rng):
+    blocks = rk.synth_q_weights(4, 64, 512, seed=4)
+    a = np.zeros((4, 512), dtype=np.float32)
+    out = np.zeros((4, 64), dtype=np.float32)
+    assert ctx.matmul_q(4, blocks, a, out, 4, 512, 64, weights_bytes=blocks.nbytes - 1) == -1
+    assert ctx.matmul_q(4, blocks, a, out, 4, 500, 64) == -1
+    assert ctx.matmul_q(4, blocks, a, out, 0, 512, 64) == -1
+    # M=1 limits of execute_cached_w8a8_m1
+    assert ctx.matmul_q(4, rk.synth_q_weights(4, 64, 256, 1), a[:1, :256].copy(), out[:1], 1, 256, 64) == -1
+
+
+def test_capi_concat_group_equals_separate(ctx, rng):
+    m, k = 64, 2048
+    ns, kinds = [2048, 256, 256], [4, 4, 6]
+    ws = [rk.synth_q_weights(kd, n, k, seed=20 + i) for i, (kd, n) in enumerate(zip(kinds, ns))]
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    outs = [np.empty((m, n), dtype=np.float32) for n in ns]
+    assert ctx.matmul_q_concat(ws, kinds, ns, a, outs, m, k) == 0
+    for w, kd, n, o in zip(ws, kinds, ns, outs):
+        st, ref = oracle.matmul_q(kd, w, a, n)
+        assert np.array_equal(_bits(o), _bits(ref))
+
+
+def test_capi_f16_executor(ctx, rng):
+    m, k, n = 33, 1000, 80
+    w = (rng.standard_normal((n, k)) * 0.05).astype(np.float16)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    out = np.empty((m, n), dtype=np.float32)
+    assert ctx.matmul_f16(w.view(np.uint16), a, out, m, k, n) == 0
+    ref = oracle.matmul_f16(w.view(np.uint16), a)
+    np.testing.assert_allclose(out, ref, rtol=1e-3, atol=1e-3 * np.abs(ref).max())
+
+
+def test_capi_w8a8_m1_pair_triple(ctx, rng):
+    k = 2048
+    ns = [2048, 256, 256]
+    ws = [rng.integers(-127, 128, size=(n, k), dtype=np.int8) for n in ns]
+    ss = [rng.uniform(0.001, 0.01, size=n).astype(np.float32) for n in ns]
+    a = rng.standard_normal(k).astype(np.float32)
+    refs = [oracle.matmul_w8a8(w, s, a.reshape(1, k))[1].reshape(-1) for w, s in zip(ws, ss)]
+    before = ctx.decode_cache_stats()
+    o = np.empty(ns[0], dtype=np.float32)
+    assert ctx.matmul_w8a8_m1(ws[0], ss[0], a, o, k, ns[0]) == 0
+    assert np.array_equal(_bits(o), _bits(refs[0]))
+    o1, o2 = np.empty(ns[0], np.float32), np.empty(ns[1], np.float32)
+    assert ctx.matmul_w8a8_pair_m1(ws[0], ss[0], ns[0], ws[1], ss[1], ns[1], a, o1, o2, k) == 0
+    assert np.array_equal(_bits(o1), _bits(refs[0])) and np.array_equal(_bits(o2), _bits(refs[1]))
+    t = [np.empty(n, np.float32) for n in ns]
+    assert ctx.matmul_w8a8_triple_m1(ws[0], ss[0], ns[0], ws[1], ss[1], ns[1], ws[2], ss[2], ns[2], a, *t, k) == 0
+    for x, r in zip(t, refs):
+        assert np.array_equal(_bits(x), _bits(r))
+    st = ctx.decode_cache_stats()
+    assert st.entries - before.entries == 3 and st.misses - before.misses == 3
+    assert ctx.matmul_w8a8_m1(ws[0], ss[0], a, o, k, ns[0]) == 0
+    assert ctx.decode_cache_stats().hits == st.hits + 1
+
+
+def test_capi_w8a8_m16(ctx, rng):
+    k, n = 2048, 512
+    w = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
+    s = rng.uniform(0.001, 0.01, size=n).astype(np.float32)
+    a = rng.standard_normal((16, k)).astype(np.float32)
+    out = np.empty((16, n), dtype=np.float32)
+    assert ctx.matmul_w8a8_m16(w, s, a, out, k, n) == 0
+    assert np.array_equal(_bits(out), _bits(oracle.matmul_w8a8(w, s, a)[1]))
