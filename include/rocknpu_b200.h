@@ -85,11 +85,20 @@ int rocknpu_b200_prepare_w8(uint32_t kind, const uint8_t *blocks, size_t k, size
 int rocknpu_b200_quantize_rows(const float *a, size_t m, size_t k, int8_t *a_i8, size_t ld_i8, float *scales,
                                int *status, rocknpu_stream stream);
 
+/* Bytes of split-K workspace the W8A8 GEMM of this shape can use (0: the
+ * shape runs without K splits). */
+size_t rocknpu_b200_gemm_workspace_bytes(size_t m, size_t n, size_t k);
+
 /* K3: out[m][ldo] = (f32(acc) * a_scales[m]) * w_scales[n], acc = exact int32
- * sum_k a_i8[m][k] * w_i8[n][k]; acc_out (optional, [m][n]) receives acc. */
+ * sum_k a_i8[m][k] * w_i8[n][k]; acc_out (optional, [m][n]) receives acc.
+ * `workspace` (optional, device memory, all-zero before its first use; every
+ * launch leaves it all-zero) lets short-M shapes split K across CTAs; NULL or
+ * fewer than rocknpu_b200_gemm_workspace_bytes bytes runs without splits.
+ * Launches that share a workspace must not overlap on the GPU. */
 int rocknpu_b200_gemm_w8a8(const int8_t *a_i8, size_t ld_a, const float *a_scales, const int8_t *w_i8,
                            size_t ld_w, const float *w_scales, float *out, size_t ldo, int32_t *acc_out, size_t m,
-                           size_t k, size_t n, int *status, rocknpu_stream stream);
+                           size_t k, size_t n, void *workspace, size_t workspace_bytes, int *status,
+                           rocknpu_stream stream);
 
 /* K2 + K3 (+ K5 for m == 1) through the context's workspace: the whole
  * W8A8 MUL_MAT on resident f32 activations and resident prepared weights. */

@@ -64,7 +64,8 @@ SIGNATURES = {
     "rocknpu_b200_context_check": (_I, [_P]),
     "rocknpu_b200_prepare_w8": (_I, [_U32, _P, _S, _S, _P, _P, _P, _P]),
     "rocknpu_b200_quantize_rows": (_I, [_P, _S, _S, _P, _S, _P, _P, _P]),
-    "rocknpu_b200_gemm_w8a8": (_I, [_P, _S, _P, _P, _S, _P, _P, _S, _P, _S, _S, _S, _P, _P]),
+    "rocknpu_b200_gemm_workspace_bytes": (_S, [_S, _S, _S]),
+    "rocknpu_b200_gemm_w8a8": (_I, [_P, _S, _P, _P, _S, _P, _P, _S, _P, _S, _S, _S, _P, _S, _P, _P]),
     "rocknpu_b200_matmul_w8a8": (_I, [_P, _P, _P, _P, _P, _S, _S, _S, _P]),
     "rocknpu_b200_gemm_f16": (_I, [_P, _S, _P, _S, _P, _S, _S, _S, _S, _P, _P]),
     "rocknpu_b200_gemv_w8a8": (_I, [_P, _P, _P, _P, _P, _S, _S, _P]),

@@ -69,6 +69,23 @@ bool mtile_rows(size_t m) {  // MTILE_ROWS (L:1992)
 
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// Split-K workspace of one GEMM inside a caller- or context-owned buffer:
+// tile counters first (256-byte aligned), then the int32 partial sums.
+size_t gemm_ws_bytes(const rk::GemmPlan& pl) {
+    if (pl.ksplit <= 1) return 0;
+    return round_up(pl.counter_elems * sizeof(unsigned), 256) + pl.ws_elems * sizeof(int32_t);
+}
+
+rk::GemmWorkspace gemm_ws_view(void* base, size_t bytes, const rk::GemmPlan& pl) {
+    rk::GemmWorkspace w;
+    if (pl.ksplit <= 1 || !base || bytes < gemm_ws_bytes(pl)) return w;
+    w.counters = static_cast<unsigned*>(base);
+    w.counter_elems = pl.counter_elems;
+    w.ws = reinterpret_cast<int32_t*>(static_cast<char*>(base) + round_up(pl.counter_elems * sizeof(unsigned), 256));
+    w.ws_elems = pl.ws_elems;
+    return w;
+}
+
 // Column chunk width of split_wide_mtile (L:2140-2141) for n > 8192.
 size_t wide_chunk(size_t n) {
     const size_t chunks = (n + 8191) / 8192;
@@ -135,6 +152,7 @@ Route route_q5_prompt(size_t m, size_t k, size_t n) {
 struct DevBuf {
     void* ptr = nullptr;
     size_t cap = 0;
+    bool zeroed = false;  // keep the buffer all-zero on (re)allocation
     cudaError_t ensure(size_t bytes) {
         if (bytes <= cap) return cudaSuccess;
         if (ptr) cudaFree(ptr);
@@ -143,6 +161,11 @@ struct DevBuf {
         const size_t want = std::max(bytes, round_up(bytes + bytes / 4, 1 << 20));
         cudaError_t e = cudaMalloc(&ptr, want);
         if (e != cudaSuccess) {
+            ptr = nullptr;
+            return e;
+        }
+        if (zeroed && (e = cudaMemset(ptr, 0, want)) != cudaSuccess) {
+            cudaFree(ptr);
             ptr = nullptr;
             return e;
         }
@@ -209,13 +232,18 @@ uint64_t now_ns() {
 
 struct RockNpuContext {
     int device = 0;
-    cudaStream_t stream = nullptr;
+    cudaStream_t stream = nullptr;   // kernels
+    cudaStream_t h2d = nullptr;      // host -> device copies of activation chunks
+    cudaStream_t d2h = nullptr;      // device -> host copies of output chunks
+    static constexpr int kMaxChunks = 16;
+    cudaEvent_t ev_in[kMaxChunks] = {}, ev_out[kMaxChunks] = {};
     bool direct_submit = false;  // ROCKNPU_W8_DIRECT_SUBMIT at creation (int8_decode_pool.rs:509)
 
     int* d_status = nullptr;  // device error word
     int* h_status = nullptr;  // pinned mirror
 
     DevBuf a_f32, a_i8, a_scale, a_f16, out_f32, staging, swiglu_tmp;
+    DevBuf gemm_ws;  // split-K workspace, all-zero between launches
 
     // Prompt-path (M-tile) resident weights: single projections and
     // concatenated same-input groups (L:1808-1849, L:2351-2384).
@@ -256,7 +284,21 @@ int finish(Ctx* c) {
     if (e != cudaSuccess) return kExecError;
     const int s = *c->h_status;
     if (s == rk::kErrNone) return kOk;
+    // a launch that stopped early may leave split-K partials behind
+    if (s != rk::kErrNonFinite && c->gemm_ws.ptr) cudaMemset(c->gemm_ws.ptr, 0, c->gemm_ws.cap);
+    cudaMemset(c->d_status, 0, sizeof(int));
     return s == rk::kErrNonFinite ? kInvalid : kExecError;
+}
+
+// Context split-K workspace sized for a W8A8 GEMM of this shape.
+int context_ws(Ctx* c, size_t m, size_t n, size_t k, rk::GemmWorkspace* out) {
+    const rk::GemmPlan pl = rk::plan_gemm(0, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k));
+    const size_t bytes = gemm_ws_bytes(pl);
+    *out = rk::GemmWorkspace{};
+    if (bytes == 0) return kOk;
+    if (c->gemm_ws.ensure(bytes) != cudaSuccess) return kExecError;
+    *out = gemm_ws_view(c->gemm_ws.ptr, c->gemm_ws.cap, pl);
+    return kOk;
 }
 
 int reset_status(Ctx* c) { return cuda_status(cudaMemsetAsync(c->d_status, 0, sizeof(int), c->stream)); }
@@ -320,8 +362,19 @@ struct OutSeg {
     size_t n;
 };
 
-// Queue quantisation + GEMM (or GEMV for m == 1) of host activations
-// against a resident int8 weight, then copy the member outputs back.
+// Rows per pipeline chunk of a host-pointer call: the activation copy of
+// chunk i+1, the kernels of chunk i and the output copy of chunk i-1 run
+// concurrently (rows are independent: per-token scales, per-row outputs).
+size_t chunk_rows(size_t m) {
+    if (m <= 64) return m;
+    const size_t want = std::max<size_t>(64, round_up((m + 7) / 8, 16));
+    return std::min(m, std::max(want, round_up((m + RockNpuContext::kMaxChunks - 1) / RockNpuContext::kMaxChunks, 16)));
+}
+
+// Quantisation + GEMM (GEMV for m == 1) of host activations against a
+// resident int8 weight, member outputs copied back, pipelined over row
+// chunks on three streams.  On INVALID_ARGUMENT (a non-finite activation)
+// output rows of chunks that were already copied back hold their results.
 int run_w8a8(Ctx* c, const PreparedW8& pw, const float* host_a, size_t m, size_t k, const OutSeg* segs, size_t nseg,
              bool m1_overlap) {
     const size_t ld8 = round_up(k, 16);
@@ -331,51 +384,86 @@ int run_w8a8(Ctx* c, const PreparedW8& pw, const float* host_a, size_t m, size_t
         return kExecError;
     int st = reset_status(c);
     if (st != kOk) return st;
-    if (cudaMemcpyAsync(c->a_f32.ptr, host_a, m * k * sizeof(float), cudaMemcpyHostToDevice, c->stream))
-        return kExecError;
-    rk::launch_quant_rows(c->a_f32.as<float>(), static_cast<int>(m), static_cast<int>(k), static_cast<long long>(k),
-                          c->a_i8.as<int8_t>(), static_cast<long long>(ld8), c->a_scale.as<float>(), c->d_status,
-                          c->stream);
     float* out = c->out_f32.as<float>();
+    float* a_dev = c->a_f32.as<float>();
+    int8_t* a8 = c->a_i8.as<int8_t>();
+    float* as = c->a_scale.as<float>();
+
     if (m == 1 && k % 16 == 0) {
-        rk::launch_gemv_w8a8(pw.w, pw.scales, c->a_i8.as<int8_t>(), c->a_scale.as<float>(), static_cast<int>(k),
-                             static_cast<int>(total_n), out, c->stream);
+        if (cudaMemcpyAsync(a_dev, host_a, k * sizeof(float), cudaMemcpyHostToDevice, c->stream)) return kExecError;
+        rk::launch_quant_rows(a_dev, 1, static_cast<int>(k), static_cast<long long>(k), a8,
+                              static_cast<long long>(ld8), as, c->d_status, c->stream);
+        rk::launch_gemv_w8a8(pw.w, pw.scales, a8, as, static_cast<int>(k), static_cast<int>(total_n), out, c->stream);
         if (cudaGetLastError() != cudaSuccess) return kExecError;
-    } else {
+        if (m1_overlap && c->overlap) {
+            // one-shot host work while the GPU runs (take_overlap, L:264-273)
+            rocknpu_overlap_fn fn = c->overlap;
+            void* user = c->overlap_user;
+            c->overlap = nullptr;
+            c->overlap_user = nullptr;
+            fn(user);
+        }
+        st = finish(c);
+        if (st != kOk) return st;
+        size_t start = 0;
+        for (size_t i = 0; i < nseg; ++i) {
+            if (cudaMemcpyAsync(segs[i].host, out + start, segs[i].n * sizeof(float), cudaMemcpyDeviceToHost,
+                                c->stream))
+                return kExecError;
+            start += segs[i].n;
+        }
+        return cuda_status(cudaStreamSynchronize(c->stream));
+    }
+
+    rk::GemmWorkspace gws;
+    const size_t rows = chunk_rows(m);
+    // the pipeline reuses one split-K workspace per chunk: size it for the
+    // largest chunk (stream order keeps chunk launches from overlapping)
+    if (context_ws(c, rows, total_n, k, &gws) != kOk) return kExecError;
+    int chunk = 0;
+    for (size_t r0 = 0; r0 < m; r0 += rows, ++chunk) {
+        const size_t mr = std::min(rows, m - r0);
+        cudaEvent_t ein = c->ev_in[chunk % RockNpuContext::kMaxChunks];
+        cudaEvent_t eout = c->ev_out[chunk % RockNpuContext::kMaxChunks];
+        if (chunk >= RockNpuContext::kMaxChunks) return kExecError;  // chunk_rows bounds the count
+        if (cudaMemcpyAsync(a_dev + r0 * k, host_a + r0 * k, mr * k * sizeof(float), cudaMemcpyHostToDevice, c->h2d) ||
+            cudaEventRecord(ein, c->h2d) || cudaStreamWaitEvent(c->stream, ein, 0))
+            return kExecError;
+        rk::launch_quant_rows(a_dev + r0 * k, static_cast<int>(mr), static_cast<int>(k), static_cast<long long>(k),
+                              a8 + r0 * ld8, static_cast<long long>(ld8), as + r0, c->d_status, c->stream);
         rk::OutMembers om;
         om.count = static_cast<int>(nseg);
         size_t start = 0;
         for (size_t i = 0; i < nseg; ++i) {
             om.n_start[i] = static_cast<int>(start);
-            om.out[i] = out + m * start;
+            om.out[i] = out + m * start + r0 * segs[i].n;
             om.ldo[i] = static_cast<long long>(segs[i].n);
             start += segs[i].n;
         }
         om.n_start[nseg] = static_cast<int>(start);
-        const int e = rk::launch_gemm_tc(0, pw.w, static_cast<long long>(pw.k), c->a_i8.ptr,
-                                         static_cast<long long>(ld8), static_cast<int>(m), static_cast<int>(total_n),
-                                         static_cast<int>(k), pw.scales, c->a_scale.as<float>(), om, nullptr, 0,
-                                         c->d_status, c->stream);
-        if (e != cudaSuccess) return kExecError;
-    }
-    if (m1_overlap && c->overlap) {
-        // one-shot host work while the GPU runs (take_overlap, L:264-273)
-        rocknpu_overlap_fn fn = c->overlap;
-        void* user = c->overlap_user;
-        c->overlap = nullptr;
-        c->overlap_user = nullptr;
-        fn(user);
+        const int e = rk::launch_gemm_tc(0, pw.w, static_cast<long long>(pw.k), a8 + r0 * ld8,
+                                         static_cast<long long>(ld8), static_cast<int>(mr), static_cast<int>(total_n),
+                                         static_cast<int>(k), pw.scales, as + r0, om, nullptr, 0, c->d_status,
+                                         c->stream, &gws);
+        if (e != cudaSuccess || cudaEventRecord(eout, c->stream) || cudaStreamWaitEvent(c->d2h, eout, 0))
+            return kExecError;
+        if (rows >= m) {
+            // one chunk: check the status first so a rejected call leaves
+            // the caller's output untouched, as the reference does
+            st = finish(c);
+            if (st != kOk) return st;
+        }
+        start = 0;
+        for (size_t i = 0; i < nseg; ++i) {
+            if (cudaMemcpyAsync(segs[i].host + r0 * segs[i].n, out + m * start + r0 * segs[i].n,
+                                mr * segs[i].n * sizeof(float), cudaMemcpyDeviceToHost, c->d2h))
+                return kExecError;
+            start += segs[i].n;
+        }
     }
     st = finish(c);
-    if (st != kOk) return st;
-    size_t start = 0;
-    for (size_t i = 0; i < nseg; ++i) {
-        if (cudaMemcpyAsync(segs[i].host, out + m * start, m * segs[i].n * sizeof(float), cudaMemcpyDeviceToHost,
-                            c->stream))
-            return kExecError;
-        start += segs[i].n;
-    }
-    return cuda_status(cudaStreamSynchronize(c->stream));
+    const int st2 = cuda_status(cudaStreamSynchronize(c->d2h));
+    return st != kOk ? st : st2;
 }
 
 // FP16 executor on resident f16 rows: f16(a) . w^T in f32.
@@ -631,7 +719,14 @@ rocknpu_context* rocknpu_context_create(void) {
     c->device = dev;
     c->direct_submit = std::getenv("ROCKNPU_W8_DIRECT_SUBMIT") != nullptr;
     c->profile = env_enabled("ROCKNPU_MTILE_PROFILE");
-    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+    c->gemm_ws.zeroed = true;
+    bool events_ok = true;
+    for (int i = 0; i < RockNpuContext::kMaxChunks && events_ok; ++i)
+        events_ok = cudaEventCreateWithFlags(&c->ev_in[i], cudaEventDisableTiming) == cudaSuccess &&
+                    cudaEventCreateWithFlags(&c->ev_out[i], cudaEventDisableTiming) == cudaSuccess;
+    if (!events_ok || cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&c->h2d, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&c->d2h, cudaStreamNonBlocking) != cudaSuccess ||
         cudaMalloc(&c->d_status, sizeof(int)) != cudaSuccess ||
         cudaHostAlloc(&c->h_status, sizeof(int), cudaHostAllocDefault) != cudaSuccess ||
         cudaMemset(c->d_status, 0, sizeof(int)) != cudaSuccess) {
@@ -679,10 +774,17 @@ void rocknpu_context_destroy(rocknpu_context* context) {
     c->decode.clear();
     c->decode_groups.clear();
     c->f16.clear();
-    for (DevBuf* b : {&c->a_f32, &c->a_i8, &c->a_scale, &c->a_f16, &c->out_f32, &c->staging, &c->swiglu_tmp})
+    for (DevBuf* b : {&c->a_f32, &c->a_i8, &c->a_scale, &c->a_f16, &c->out_f32, &c->staging, &c->swiglu_tmp,
+                      &c->gemm_ws})
         b->release();
     if (c->d_status) cudaFree(c->d_status);
     if (c->h_status) cudaFreeHost(c->h_status);
+    for (int i = 0; i < RockNpuContext::kMaxChunks; ++i) {
+        if (c->ev_in[i]) cudaEventDestroy(c->ev_in[i]);
+        if (c->ev_out[i]) cudaEventDestroy(c->ev_out[i]);
+    }
+    if (c->h2d) cudaStreamDestroy(c->h2d);
+    if (c->d2h) cudaStreamDestroy(c->d2h);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
 }
@@ -999,9 +1101,14 @@ int rocknpu_b200_quantize_rows(const float* a, size_t m, size_t k, int8_t* a_i8,
     return cuda_status(cudaGetLastError());
 }
 
+size_t rocknpu_b200_gemm_workspace_bytes(size_t m, size_t n, size_t k) {
+    if (m == 0 || n == 0 || k == 0 || m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff) return 0;
+    return gemm_ws_bytes(rk::plan_gemm(0, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k)));
+}
+
 int rocknpu_b200_gemm_w8a8(const int8_t* a_i8, size_t ld_a, const float* a_scales, const int8_t* w_i8, size_t ld_w,
                            const float* w_scales, float* out, size_t ldo, int32_t* acc_out, size_t m, size_t k,
-                           size_t n, int* status, rocknpu_stream stream) {
+                           size_t n, void* workspace, size_t workspace_bytes, int* status, rocknpu_stream stream) {
     if (!a_i8 || !a_scales || !w_i8 || !w_scales || !out || !status || m == 0 || k == 0 || n == 0 || ld_a < k ||
         ld_w < k || ldo < n || m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff)
         return kInvalid;
@@ -1010,9 +1117,12 @@ int rocknpu_b200_gemm_w8a8(const int8_t* a_i8, size_t ld_a, const float* a_scale
     om.n_start[1] = static_cast<int>(n);
     om.out[0] = out;
     om.ldo[0] = static_cast<long long>(ldo);
+    const rk::GemmWorkspace gws = gemm_ws_view(
+        workspace, workspace_bytes, rk::plan_gemm(0, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k)));
     const int e = rk::launch_gemm_tc(0, w_i8, static_cast<long long>(ld_w), a_i8, static_cast<long long>(ld_a),
                                      static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), w_scales, a_scales,
-                                     om, acc_out, static_cast<long long>(n), status, static_cast<cudaStream_t>(stream));
+                                     om, acc_out, static_cast<long long>(n), status, static_cast<cudaStream_t>(stream),
+                                     &gws);
     return e == cudaSuccess ? kOk : (e == cudaErrorInvalidValue ? kInvalid : kExecError);
 }
 
@@ -1031,8 +1141,17 @@ int rocknpu_b200_matmul_w8a8(rocknpu_context* context, const float* a, const int
                              static_cast<int>(k), static_cast<int>(n), out, s);
         return cuda_status(cudaGetLastError());
     }
-    return rocknpu_b200_gemm_w8a8(context->a_i8.as<int8_t>(), ld8, context->a_scale.as<float>(), w_i8, k, w_scales,
-                                  out, n, nullptr, m, k, n, context->d_status, s);
+    rk::GemmWorkspace gws;
+    if (context_ws(context, m, n, k, &gws) != kOk) return kExecError;
+    rk::OutMembers om;
+    om.count = 1;
+    om.n_start[1] = static_cast<int>(n);
+    om.out[0] = out;
+    om.ldo[0] = static_cast<long long>(n);
+    const int e = rk::launch_gemm_tc(0, w_i8, static_cast<long long>(k), context->a_i8.ptr, static_cast<long long>(ld8),
+                                     static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), w_scales,
+                                     context->a_scale.as<float>(), om, nullptr, 0, context->d_status, s, &gws);
+    return e == cudaSuccess ? kOk : kExecError;
 }
 
 int rocknpu_b200_gemm_f16(const uint16_t* a_f16, size_t ld_a, const uint16_t* w_f16, size_t ld_w, float* out,

@@ -36,14 +36,32 @@ void launch_quant_rows(const float* a, int m, int k, long long lda, int8_t* a8, 
 // FP16 executor input: f32 [m, k] -> f16 [m, ldo] (round to nearest even).
 void launch_f32_to_f16(const float* a, int m, int k, long long lda, __half* out, long long ldo, cudaStream_t s);
 
+// Split-K workspace of the W8A8 GEMM: int32 partial sums [m][n] and one
+// arrival counter per output tile.  Both must be all-zero before the first
+// launch; every launch leaves them all-zero again.
+struct GemmWorkspace {
+    int32_t* ws = nullptr;
+    unsigned* counters = nullptr;
+    size_t ws_elems = 0, counter_elems = 0;
+};
+
+// Tile plan of one GEMM launch: token tile height, K splits and the
+// workspace a split launch needs.
+struct GemmPlan {
+    int bt = 128, ksplit = 1, kb_per_split = 1, tiles = 1;
+    size_t ws_elems = 0, counter_elems = 0;
+};
+GemmPlan plan_gemm(int kind, int m, int n, int k);
+
 // K3/K4: out = epilogue(W[n,k] . A[m,k]^T) on tcgen05.  kind 0: int8 inputs,
 // int32 accumulators, out = (f32(acc) * a_scale[m]) * w_scale[n]; kind 1:
 // f16 inputs, f32 accumulators, out = acc.  ld*_bytes are row pitches
 // (multiples of 16).  acc_out (kind 0, optional) receives the raw int32.
 // Returns a cudaError_t value.
+// A null or too small `ws` runs the launch without K splits.
 int launch_gemm_tc(int kind, const void* w, long long ldw_bytes, const void* a, long long lda_bytes, int m, int n,
                    int k, const float* w_scale, const float* a_scale, const OutMembers& outs, int32_t* acc_out,
-                   long long acc_ld, int* err, cudaStream_t s);
+                   long long acc_ld, int* err, cudaStream_t s, const GemmWorkspace* ws = nullptr);
 
 // K5: M=1 W8A8 GEMV over resident int8 rows.
 void launch_gemv_w8a8(const int8_t* w, const float* w_scale, const int8_t* a8, const float* a_scale, int k, int n,

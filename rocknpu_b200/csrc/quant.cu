@@ -191,6 +191,9 @@ __global__ void __launch_bounds__(kRowThreads) quant_rows_kernel(const float* __
                                                                   int* __restrict__ err) {
     extern __shared__ __align__(16) float srow[];
     __shared__ float red[33];
+    // let the dependent GEMM launch now: it sets up and streams weights while
+    // this kernel runs, and waits (griddepcontrol.wait) before reading our output
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int row = blockIdx.x;
     const float* src = a + static_cast<size_t>(row) * lda;
     const int k16 = (k + 15) & ~15;

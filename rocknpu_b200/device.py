@@ -48,16 +48,28 @@ def quantize_rows(a: torch.Tensor, status: torch.Tensor, out: torch.Tensor | Non
     return out, scales
 
 
+def workspace_bytes(m: int, n: int, k: int) -> int:
+    return int(lib().rocknpu_b200_gemm_workspace_bytes(m, n, k))
+
+
+def new_workspace(nbytes: int, device=None) -> torch.Tensor:
+    """Zeroed split-K workspace (the GEMM keeps it zero between launches)."""
+    return torch.zeros(max(nbytes, 1), dtype=torch.uint8, device=device or "cuda")
+
+
 def gemm_w8a8(a8: torch.Tensor, a_scales: torch.Tensor, w8: torch.Tensor, w_scales: torch.Tensor,
-              status: torch.Tensor, out: torch.Tensor | None = None, acc: torch.Tensor | None = None, stream=None):
+              status: torch.Tensor, out: torch.Tensor | None = None, acc: torch.Tensor | None = None,
+              workspace: torch.Tensor | None = None, stream=None):
     """K3: (f32(acc) * a_s) * w_s with acc = a8 . w8^T exact int32."""
     m, k = a8.shape
     n = w8.shape[0]
     out = torch.empty((m, n), dtype=torch.float32, device=a8.device) if out is None else out
+    ws_ptr = workspace.data_ptr() if workspace is not None else None
+    ws_bytes = workspace.numel() if workspace is not None else 0
     _check(lib().rocknpu_b200_gemm_w8a8(a8.data_ptr(), a8.stride(0), a_scales.data_ptr(), w8.data_ptr(),
                                         w8.stride(0), w_scales.data_ptr(), out.data_ptr(), out.stride(0),
-                                        acc.data_ptr() if acc is not None else None, m, k, n, status.data_ptr(),
-                                        _stream(stream)), "gemm_w8a8")
+                                        acc.data_ptr() if acc is not None else None, m, k, n, ws_ptr, ws_bytes,
+                                        status.data_ptr(), _stream(stream)), "gemm_w8a8")
     return out
 
 

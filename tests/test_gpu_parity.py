@@ -119,25 +119,30 @@ GEMM_SHAPES = [
 ]
 
 
+@pytest.mark.parametrize("split", [False, True])
 @pytest.mark.parametrize("m,k,n", GEMM_SHAPES)
-def test_gemm_w8a8_int32_exact(dev, rng, m, k, n):
+def test_gemm_w8a8_int32_exact(dev, rng, m, k, n, split):
     a8 = rng.integers(-127, 128, size=(m, k), dtype=np.int8)
     w8 = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
     a_s = rng.uniform(0.001, 0.1, size=m).astype(np.float32)
     w_s = rng.uniform(0.001, 0.1, size=n).astype(np.float32)
     acc_ref = oracle.gemm_i8_i32(a8, w8)
-    status = dev.new_status()
-    acc = torch.empty((m, n), dtype=torch.int32, device="cuda")
-    out = dev.gemm_w8a8(torch.from_numpy(a8).cuda(), torch.from_numpy(a_s).cuda(), torch.from_numpy(w8).cuda(),
-                        torch.from_numpy(w_s).cuda(), status, acc=acc)
-    torch.cuda.synchronize()
-    assert status.item() == 0
-    assert np.array_equal(acc.cpu().numpy(), acc_ref)
     exp = np.empty((m, n), dtype=np.float32)
     for r in range(m):
         oracle.lib().orc_rescale_i32_row(oracle._p(np.ascontiguousarray(acc_ref[r])), oracle._p(w_s),
                                          float(a_s[r]), oracle._p(exp[r]), n)
-    assert np.array_equal(_bits(out.cpu().numpy()), _bits(exp))
+    ws = dev.new_workspace(dev.workspace_bytes(m, n, k)) if split else None
+    ta8, tas, tw8, tws = (torch.from_numpy(x).cuda() for x in (a8, a_s, w8, w_s))
+    for _ in range(2 if split else 1):  # a split-K workspace is left zero for the next launch
+        status = dev.new_status()
+        acc = torch.empty((m, n), dtype=torch.int32, device="cuda")
+        out = dev.gemm_w8a8(ta8, tas, tw8, tws, status, acc=acc, workspace=ws)
+        torch.cuda.synchronize()
+        assert status.item() == 0
+        assert np.array_equal(acc.cpu().numpy(), acc_ref)
+        assert np.array_equal(_bits(out.cpu().numpy()), _bits(exp))
+    if split:
+        assert not ws.any().item()
 
 
 @pytest.mark.parametrize("m", [4, 8, 12, 16, 32, 48, 64, 128])
@@ -187,7 +192,7 @@ def test_gemv_decode_m1_kat(dev):
 
 @pytest.mark.parametrize("kind", [4, 6])
 @pytest.mark.parametrize("m,k,n", [(128, 2048, 5632), (1, 2048, 256), (5, 512, 64), (16, 2048, 2048),
-                                   (300, 2048, 96), (77, 5632, 256), (8, 2304, 128)])
+                                   (300, 2048, 96), (77, 5632, 256), (8, 2304, 128), (1000, 2048, 640)])
 def test_capi_matmul_q_bit_exact(ctx, rng, kind, m, k, n):
     blocks = rk.synth_q_weights(kind, n, k, seed=11 + m)
     a = rng.standard_normal((m, k)).astype(np.float32)
