@@ -105,6 +105,30 @@ int rocknpu_b200_gemm_w8a8(const int8_t *a_i8, size_t ld_a, const float *a_scale
 int rocknpu_b200_matmul_w8a8(rocknpu_context *context, const float *a, const int8_t *w_i8, const float *w_scales,
                              float *out, size_t m, size_t k, size_t n, rocknpu_stream stream);
 
+/* The same W8A8 MUL_MAT as rocknpu_b200_matmul_w8a8, for callers that may not
+ * allocate GPU memory once they are running: a runtime whose memory plan is
+ * fixed at start-up, code that runs while a stream is being captured into a
+ * CUDA graph (cudaMalloc is not allowed there), or a framework whose own
+ * allocator must own every byte.  This entry point has no counterpart in the
+ * reference interface.  It needs no context and calls no cudaMalloc,
+ * cudaFree or allocating library routine: the int8 activations, per-token
+ * scales and split-K sums live in a 16 MiB array inside the library's device
+ * memory, which every GPU that loads the library holds until the process
+ * exits.  Limit: m * round_up(k, 16) + 4 * m (each rounded up to 256 bytes)
+ * must fit in those 16 MiB, e.g. m = 2047 at k = 8192; larger calls return
+ * ROCKNPU_STATUS_INVALID_ARGUMENT and print the sizes to stderr.
+ * All pointers are device pointers on the current device; `status` (device,
+ * one int) is cleared by the call and set by the kernels like the other
+ * device entry points' status words.  Work is queued on `stream` and the
+ * call returns without waiting.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress) with that device current;
+ * make that first call before any stream capture.  Every call on a device
+ * shares the one array, which keeps the last call's contents: calls whose
+ * work overlaps on the GPU (other streams, other host threads) race and must
+ * be serialised by the caller. */
+int rocknpu_b200_matmul_w8a8_noalloc(const float *a, const int8_t *w_i8, const float *w_scales, float *out,
+                                     size_t m, size_t k, size_t n, int *status, rocknpu_stream stream);
+
 /* K4: out[m][ldo] = sum_k f16(a)[m][k] * w_f16[n][k] in f32 on tcgen05;
  * a_f16 row pitch ld_a elements (multiple of 8). */
 int rocknpu_b200_gemm_f16(const uint16_t *a_f16, size_t ld_a, const uint16_t *w_f16, size_t ld_w, float *out,
