@@ -45,10 +45,10 @@ struct GemmWorkspace {
     size_t ws_elems = 0, counter_elems = 0;
 };
 
-// Tile plan of one GEMM launch: token tile height, K splits and the
-// workspace a split launch needs.
+// Tile plan of one GEMM launch: weight tile rows, token tile height, K
+// splits and the workspace a split launch needs.
 struct GemmPlan {
-    int bt = 128, ksplit = 1, kb_per_split = 1, tiles = 1;
+    int wt = 128, bt = 128, ksplit = 1, kb_per_split = 1, tiles = 1;
     size_t ws_elems = 0, counter_elems = 0;
 };
 GemmPlan plan_gemm(int kind, int m, int n, int k);
