@@ -31,7 +31,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -85,57 +84,68 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons during the timed region."""
+    """SM clocks and clock-event (throttle) reasons sampled through NVML every
+    2 ms during the timed region (nvidia-smi as a fallback)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines = []
+    def __init__(self, cuda_index: int):
+        self.cuda_index = cuda_index
+        self.samples = []  # (time, sm MHz, reason bits)
+        self.max_mhz = None
+        self._stop = threading.Event()
+
+    def _handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        try:
+            idx = torch.cuda._get_nvml_device_index(self.cuda_index)
+        except Exception:
+            idx = self.cuda_index
+        return pynvml, pynvml.nvmlDeviceGetHandleByIndex(idx)
+
+    def _run(self):
+        try:
+            nv, h = self._handle()
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            getr = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            while not self._stop.is_set():
+                t = time.perf_counter()
+                mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                r = getr(h)
+                self.samples.append((t, mhz, r))
+                time.sleep(0.002)
+        except Exception as exc:  # no NVML: leave the record empty but say why
+            self.error = repr(exc)
 
     def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except Exception:
-            self.proc = None
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
+        time.sleep(0.05)
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *exc):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self._stop.set()
+        self.thread.join(timeout=5)
+
+    def mark(self, name):
+        setattr(self, name, time.perf_counter())
 
     def summary(self):
-        sm, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = max(mx, float(parts[2]))
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower().startswith("active"):
+        t0, t1 = getattr(self, "t_start", None), getattr(self, "t_end", None)
+        win = [x for x in self.samples if (t0 is None or x[0] >= t0) and (t1 is None or x[0] <= t1)]
+        reasons = set()
+        for _, _, r in win:
+            for bit, name in self.REASONS.items():
+                if r & bit:
                     reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        out = {"sm_mhz": statistics.median([x[1] for x in win]) if win else None, "sm_max_mhz": self.max_mhz,
+               "reasons": sorted(reasons), "samples": len(win)}
+        if getattr(self, "error", None):
+            out["error"] = self.error
+        return out
 
 
 # ---------------------------------------------------------------------------
@@ -243,11 +253,13 @@ def run_ours(args, rank: int, world: int):
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(torch.cuda.current_device()) as clocks:
+        clocks.mark("t_start")
         start.record()
         for _ in range(args.steps):
             graph.replay()
         end.record()
         torch.cuda.synchronize()
+        clocks.mark("t_end")
     barrier()
     ms = start.elapsed_time(end) / args.steps
     if rk.lib().rocknpu_b200_context_check(ctx.handle) != 0:

@@ -365,10 +365,15 @@ struct OutSeg {
 // Rows per pipeline chunk of a host-pointer call: the activation copy of
 // chunk i+1, the kernels of chunk i and the output copy of chunk i-1 run
 // concurrently (rows are independent: per-token scales, per-row outputs).
-size_t chunk_rows(size_t m) {
-    if (m <= 64) return m;
-    const size_t want = std::max<size_t>(64, round_up((m + 7) / 8, 16));
-    return std::min(m, std::max(want, round_up((m + RockNpuContext::kMaxChunks - 1) / RockNpuContext::kMaxChunks, 16)));
+// Chunks carry at least ~1.5 MB in their larger direction -- smaller copies
+// lose PCIe bandwidth to per-copy cost -- and there are at most kMaxChunks.
+size_t chunk_rows(size_t m, size_t k, size_t total_n) {
+    const size_t row_bytes = std::max(k, total_n) * sizeof(float);
+    const size_t min_rows = std::max<size_t>(16, ((size_t(3) << 19) + row_bytes - 1) / row_bytes);
+    size_t rows = std::max(min_rows, (m + 7) / 8);
+    rows = std::max(rows, (m + RockNpuContext::kMaxChunks - 1) / RockNpuContext::kMaxChunks);
+    rows = std::max<size_t>(round_up(rows, 16), 64);  // m <= 64: one chunk
+    return std::min(m, rows);
 }
 
 // Quantisation + GEMM (GEMV for m == 1) of host activations against a
@@ -416,7 +421,7 @@ int run_w8a8(Ctx* c, const PreparedW8& pw, const float* host_a, size_t m, size_t
     }
 
     rk::GemmWorkspace gws;
-    const size_t rows = chunk_rows(m);
+    const size_t rows = chunk_rows(m, k, total_n);
     // the pipeline reuses one split-K workspace per chunk: size it for the
     // largest chunk (stream order keeps chunk launches from overlapping)
     if (context_ws(c, rows, total_n, k, &gws) != kOk) return kExecError;
