@@ -471,6 +471,141 @@ def run_reference(args, rank: int, world: int):
     return line
 
 
+# ---------------------------------------------------------------------------
+# cfg5: the large-GEMM sharding sweep
+# ---------------------------------------------------------------------------
+
+CFG5_N, CFG5_K = 28672, 8192
+CFG5_M = (128, 1024, 4096, 16384)
+
+
+def cfg5_activations(m: int, device="cuda"):
+    """X [m, 8192] ~ N(0, 1) with 1 % of the K channels (82, picked by seed 2)
+    scaled x20: the outlier channels per-token int8 quantisation must absorb."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(1)
+    x = torch.randn(m, CFG5_K, generator=g, device=device)
+    ch = torch.from_numpy(np.random.default_rng(2).choice(CFG5_K, CFG5_K // 100, replace=False)).to(device)
+    x[:, ch] *= 20.0
+    return x
+
+
+def run_cfg5(args, rank: int, world: int):
+    """W8A8 GEMM throughput of the N=28672 x K=8192 Q4_K weight, N-sharded over
+    the ranks (strong scaling: the same GEMMs whatever the GPU count), plus the
+    M=1 decode GEMV.  Per M, one step = K2 quantisation of X on every rank +
+    the rank's tcgen05 GEMM + the all-gather of the output columns (peer
+    stores fused into the epilogue, or NCCL), so that every rank holds Y."""
+    import torch
+    import rocknpu_b200 as rk
+    from rocknpu_b200 import device as dev
+    from rocknpu_b200 import shard
+
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+    hbm_peak, bf16_peak, peak_src = load_peaks()
+    int8_peak = 2.0 * bf16_peak
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+    ms_list = [int(v) for v in args.m_list.split(",")]
+    max_m = max(ms_list)
+
+    t0 = time.time()
+    rows = shard.shard_rows(CFG5_N, world)
+    start, width = rows[rank]
+    # this rank's rows of the seeded N(0, 0.02^2) weight (counter-based
+    # generator: rows [start, start + width) are values [start*K, ...))
+    vals = rk.synth_normal(0, width * CFG5_K, 0.02, first=start * CFG5_K).reshape(width, CFG5_K)
+    blocks = rk.synth_encode(4, vals)
+    del vals
+    sm = shard.ShardedMatmul(4, blocks, CFG5_K, CFG5_N, route=args.route, max_m=max_m, blocks_are_local=True)
+    gen_s = time.time() - t0
+
+    def timed(fn, steps, warmup):
+        for _ in range(warmup):
+            fn()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        if dist is not None:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    sweep = {}
+    head = None
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        clocks.mark("t_start")
+        for m in ms_list:
+            x = cfg5_activations(m)
+            out = None
+            ms = timed(lambda: sm(x), args.steps, args.warmup)
+            a8, a_s = sm.quantize(x)
+            local = torch.empty((m, max(width, 1)), dtype=torch.float32, device="cuda")
+            gemm_ms = timed(lambda: dev.gemm_w8a8(a8, a_s, sm.w8, sm.w_scales, sm.status, out=local),
+                            args.steps, args.warmup)
+            sm.check()
+            ops = 2.0 * m * CFG5_N * CFG5_K
+            local_ops = 2.0 * m * width * CFG5_K
+            local_bytes = width * CFG5_K + m * CFG5_K + 4 * m * width + 4 * width + 4 * m
+            r = {"ms_per_step": round(ms, 4), "tops": round(ops / (ms * 1e-3) / 1e12, 1),
+                 "gemm_ms_local": round(gemm_ms, 4),
+                 "gemm_tops_local": round(local_ops / (gemm_ms * 1e-3) / 1e12, 1),
+                 "gemm_tensor_frac": round(local_ops / (gemm_ms * 1e-3) / 1e12 / int8_peak, 4),
+                 "gemm_hbm_frac": round(local_bytes / (gemm_ms * 1e-3) / 1e9 / hbm_peak, 4),
+                 "exchange_bytes_per_rank": 4 * m * width * (world - 1)}
+            sweep[str(m)] = r
+            head = (m, r)
+            del x, a8, a_s, local, out
+        # M = 1 decode GEMV (K5) over the same rows
+        x1 = cfg5_activations(1)
+        gemv_ms = timed(lambda: sm(x1), max(args.steps, 20), args.warmup)
+        a8, a_s = sm.quantize(x1)
+        o1 = torch.empty(max(width, 1), dtype=torch.float32, device="cuda")
+        gemv_local = timed(lambda: dev.gemv_w8a8(a8, a_s, sm.w8, sm.w_scales, out=o1), max(args.steps, 50),
+                           args.warmup)
+        gbytes = width * CFG5_K + 8 * width + CFG5_K + 4
+        sweep["1"] = {"ms_per_step": round(gemv_ms, 4), "gemv_us_local": round(gemv_local * 1e3, 2),
+                      "gemv_gbs_local": round(gbytes / (gemv_local * 1e-3) / 1e9, 1),
+                      "gemv_hbm_frac": round(gbytes / (gemv_local * 1e-3) / 1e9 / hbm_peak, 4)}
+        clocks.mark("t_end")
+    sm.check()
+    sm.close()
+    if rank != 0:
+        return None
+    m, r = head
+    line = {
+        "metric": f"W8A8 GEMM TOPS (cfg5 Q4_K N={CFG5_N} K={CFG5_K}, M={m}, N-sharded, Y all-gathered)",
+        "value": r["tops"], "unit": "TOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int8 (W8A8, int32 accumulate, f32 out)",
+        "data": "synthetic (seeded N(0,0.02^2) -> Q4_K weights; N(0,1) activations, 1% channels x20)",
+        "config": {"workload": "cfg5-large-gemm-sharding-sweep", "n": CFG5_N, "k": CFG5_K, "m_list": ms_list,
+                   "parallelism": f"nshard{world}" + (f"-{args.route}" if world > 1 else ""),
+                   "l2": "weights 235 MB int8 > L2 (streamed every step)"},
+        "roofline": {"bound": "tensor", "achieved": r["gemm_tops_local"], "peak": int8_peak, "unit": "TOP/s",
+                     "frac": r["gemm_tensor_frac"], "traffic": None,
+                     "kernel": "gemm_tc_kernel (K3, tcgen05 kind::i8), this rank's rows",
+                     "peak_source": f"{peak_src} (int8 = 2 x bf16_tflops)"},
+        "sweep": sweep,
+        "e2e": None,
+        "cpu_baseline": None,
+        "gpu_launches": None,
+        "clocks": clocks.summary(),
+        "setup_s": round(gen_s, 1),
+    }
+    return line
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -481,6 +616,10 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    ap.add_argument("--workload", choices=["tinyllama", "cfg5"], default="tinyllama")
+    ap.add_argument("--route", choices=["peer", "allgather"], default="peer",
+                    help="cfg5 output exchange at N > 1")
+    ap.add_argument("--m-list", default=",".join(str(m) for m in CFG5_M))
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -493,7 +632,12 @@ def main():
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     try:
-        line = run_reference(args, rank, world) if args.impl == "reference" else run_ours(args, rank, world)
+        if args.impl == "reference":
+            line = run_reference(args, rank, world)
+        elif args.workload == "cfg5":
+            line = run_cfg5(args, rank, world)
+        else:
+            line = run_ours(args, rank, world)
     finally:
         if world > 1 and args.impl == "ours":
             import torch.distributed as dist

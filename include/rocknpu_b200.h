@@ -1,6 +1,6 @@
 /*
  * rocknpu_b200.h -- what librocknpu.so adds beside the reference C ABI
- * (rocknpu.h).  Three groups:
+ * (rocknpu.h).  Four groups:
  *
  *  1. The ggml plugin's host rules (adapters/ggml-rocknpu), exported so a
  *     plugin built against ggml can call them and tests can check them
@@ -13,7 +13,9 @@
  *     (NULL = the context's own stream) and the call returns without
  *     waiting.  Kernels report errors in the device word `status`
  *     (0 = ok, 1 = non-finite input, >1 = a device-side wait ran out).
- *  3. Synthetic K-quant weights for tests and benchmarks (host only).
+ *  3. Multi-GPU N-sharding: the row split, the all-gather layout, and peer
+ *     (CUDA IPC) buffers for a GEMM whose epilogue all-gathers over NVLink.
+ *  4. Synthetic K-quant weights for tests and benchmarks (host only).
  */
 #ifndef ROCKNPU_B200_H
 #define ROCKNPU_B200_H
@@ -138,7 +140,54 @@ int rocknpu_b200_gemm_f16(const uint16_t *a_f16, size_t ld_a, const uint16_t *w_
 int rocknpu_b200_gemv_w8a8(const int8_t *a_i8, const float *a_scale, const int8_t *w_i8, const float *w_scales,
                            float *out, size_t k, size_t n, rocknpu_stream stream);
 
-/* ---- 3. synthetic K-quant weights (host) ------------------------------- */
+/* ---- 3. multi-GPU N-sharding (one process per GPU, one node) ----------- */
+
+#define ROCKNPU_B200_MAX_RANKS 16
+#define ROCKNPU_B200_IPC_HANDLE_BYTES 64
+
+/* Weight rows (output columns) of rank r: [starts[r], starts[r] + widths[r]).
+ * n / 32 blocks of 32 rows split evenly over `world` ranks, remainder blocks
+ * to the first ranks (the reference's N split over NPU cores,
+ * rocknpu-matmul/src/int8_decode_pool.rs:1484-1491, split_blocks :1505-1522).
+ * Ranks beyond the block count get width 0.  Returns the ranks with work. */
+size_t rocknpu_b200_shard_rows(size_t n, size_t world, size_t *starts, size_t *widths);
+
+/* All-gather route: rank-major src[world][m][shard_ld] (shard r at
+ * src + r * shard_elems, e.g. the output of an NCCL all-gather) ->
+ * row-major out[m][ldo] with shard r at columns [starts[r], +widths[r]). */
+int rocknpu_b200_gather_shards(const float *src, size_t shard_elems, size_t shard_ld, size_t m, size_t world,
+                               const size_t *starts, const size_t *widths, float *out, size_t ldo,
+                               rocknpu_stream stream);
+
+/* Peer route.  A peer buffer is `bytes` of device memory on the current GPU
+ * that the other ranks of the node map through CUDA IPC.  create() writes
+ * this rank's 64-byte handle; the caller exchanges the handles over any host
+ * transport (torch.distributed, a file, a socket) and passes all `world` of
+ * them, in rank order, to open(). */
+typedef struct rocknpu_b200_peer_buffer rocknpu_b200_peer_buffer;
+int rocknpu_b200_peer_buffer_create(size_t bytes, int rank, int world, void *handle_out,
+                                    rocknpu_b200_peer_buffer **out);
+int rocknpu_b200_peer_buffer_open(rocknpu_b200_peer_buffer *buffer, const void *handles);
+/* Rank r's data region as mapped in this process (NULL before open()). */
+void *rocknpu_b200_peer_buffer_ptr(rocknpu_b200_peer_buffer *buffer, int r);
+/* Device-side barrier of all ranks on `stream`: every rank's writes queued
+ * before it (peer stores included) are visible to every rank's work queued
+ * after it.  Waits are bounded (2 s); a rank that never arrives leaves
+ * status 6 in *status. */
+int rocknpu_b200_peer_barrier(rocknpu_b200_peer_buffer *buffer, int *status, rocknpu_stream stream);
+void rocknpu_b200_peer_buffer_destroy(rocknpu_b200_peer_buffer *buffer);
+
+/* K3 with the all-gather fused into the epilogue: this rank's n_local weight
+ * rows produce output columns [col0, col0 + n_local), and every element is
+ * stored into outs[0..copies) (device pointers, typically every rank's peer
+ * buffer data region: [m][ldo] f32) -- the tiles cross NVLink while the
+ * tensor cores work on the next ones.  Follow with rocknpu_b200_peer_barrier
+ * before reading the outputs. */
+int rocknpu_b200_gemm_w8a8_gather(const int8_t *a_i8, size_t ld_a, const float *a_scales, const int8_t *w_i8,
+                                  size_t ld_w, const float *w_scales, float *const *outs, size_t copies, size_t col0,
+                                  size_t ldo, size_t m, size_t k, size_t n_local, int *status, rocknpu_stream stream);
+
+/* ---- 4. synthetic K-quant weights (host) ------------------------------- */
 
 /* Deterministic N(0, sigma^2) f32 values (counter-based: value i depends only
  * on seed and i, so any slice can be generated independently). */

@@ -70,6 +70,14 @@ SIGNATURES = {
     "rocknpu_b200_matmul_w8a8_noalloc": (_I, [_P, _P, _P, _P, _S, _S, _S, _P, _P]),
     "rocknpu_b200_gemm_f16": (_I, [_P, _S, _P, _S, _P, _S, _S, _S, _S, _P, _P]),
     "rocknpu_b200_gemv_w8a8": (_I, [_P, _P, _P, _P, _P, _S, _S, _P]),
+    "rocknpu_b200_shard_rows": (_S, [_S, _S, _P, _P]),
+    "rocknpu_b200_gather_shards": (_I, [_P, _S, _S, _S, _S, _P, _P, _P, _S, _P]),
+    "rocknpu_b200_peer_buffer_create": (_I, [_S, _I, _I, _P, _P]),
+    "rocknpu_b200_peer_buffer_open": (_I, [_P, _P]),
+    "rocknpu_b200_peer_buffer_ptr": (_P, [_P, _I]),
+    "rocknpu_b200_peer_barrier": (_I, [_P, _P, _P]),
+    "rocknpu_b200_peer_buffer_destroy": (None, [_P]),
+    "rocknpu_b200_gemm_w8a8_gather": (_I, [_P, _S, _P, _P, _S, _P, _P, _S, _S, _S, _S, _S, _S, _P, _P]),
     "rocknpu_synth_normal": (None, [ctypes.c_uint64, ctypes.c_uint64, _S, ctypes.c_float, _P]),
     "rocknpu_synth_encode": (_I, [_U32, _P, _S, _S, _P]),
 }

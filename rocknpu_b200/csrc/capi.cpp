@@ -1176,6 +1176,29 @@ int rocknpu_b200_gemm_f16(const uint16_t* a_f16, size_t ld_a, const uint16_t* w_
     return e == cudaSuccess ? kOk : (e == cudaErrorInvalidValue ? kInvalid : kExecError);
 }
 
+int rocknpu_b200_gemm_w8a8_gather(const int8_t* a_i8, size_t ld_a, const float* a_scales, const int8_t* w_i8,
+                                  size_t ld_w, const float* w_scales, float* const* outs, size_t copies, size_t col0,
+                                  size_t ldo, size_t m, size_t k, size_t n_local, int* status, rocknpu_stream stream) {
+    if (!a_i8 || !a_scales || !w_i8 || !w_scales || !outs || !status || copies == 0 ||
+        copies > static_cast<size_t>(rk::kMaxCopies) || m == 0 || k == 0 || n_local == 0 || ld_a < k ||
+        ld_w < k || col0 + n_local > ldo || m > 0x7fffffff || n_local > 0x7fffffff || k > 0x7fffffff)
+        return kInvalid;
+    rk::OutMembers om;
+    om.count = 1;
+    om.n_start[1] = static_cast<int>(n_local);
+    om.ldo[0] = static_cast<long long>(ldo);
+    om.copies = static_cast<int>(copies);
+    for (size_t c = 0; c < copies; ++c) {
+        if (!outs[c]) return kInvalid;
+        om.copy_out[c] = outs[c] + col0;
+    }
+    om.out[0] = om.copy_out[0];
+    const int e = rk::launch_gemm_tc(0, w_i8, static_cast<long long>(ld_w), a_i8, static_cast<long long>(ld_a),
+                                     static_cast<int>(m), static_cast<int>(n_local), static_cast<int>(k), w_scales,
+                                     a_scales, om, nullptr, 0, status, static_cast<cudaStream_t>(stream), nullptr);
+    return e == cudaSuccess ? kOk : (e == cudaErrorInvalidValue ? kInvalid : kExecError);
+}
+
 int rocknpu_b200_gemv_w8a8(const int8_t* a_i8, const float* a_scale, const int8_t* w_i8, const float* w_scales,
                            float* out, size_t k, size_t n, rocknpu_stream stream) {
     if (!a_i8 || !a_scale || !w_i8 || !w_scales || !out || k == 0 || n == 0 || k % 16 != 0 || k > 200 * 1024 ||

@@ -70,6 +70,8 @@ struct GemmParams {
     int n_start[5];
     float* out[4];
     long long ldo[4];
+    int copies;                   // > 1: elements go to every copy_out[c] instead
+    float* copy_out[kMaxCopies];  // at out[0]'s offsets (peer all-gather)
     int32_t* acc_out;
     long long acc_ld;
     int32_t* ws;         // split-K partial sums [m][n], all zero between launches
@@ -430,10 +432,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                                     if (split) {
                                         atomicAdd(wsp + static_cast<long long>(m) * p.n + col, static_cast<int>(r[jj]));
                                     } else {
-                                        o[jj * ldo] =
+                                        const float v =
                                             __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[jj])), asv[jj]), wsc);
+                                        if (p.copies > 1) {
+                                            const long long off = static_cast<long long>(m) * ldo + ocol;
+#pragma unroll 1
+                                            for (int cp = 0; cp < p.copies; ++cp) p.copy_out[cp][off] = v;
+                                        } else {
+                                            o[jj * ldo] = v;
+                                        }
                                         if (acc_out) acc_out[static_cast<long long>(m) * p.acc_ld + col] = r[jj];
                                     }
+                                } else if (p.copies > 1) {
+                                    const long long off = static_cast<long long>(m) * ldo + ocol;
+#pragma unroll 1
+                                    for (int cp = 0; cp < p.copies; ++cp) p.copy_out[cp][off] = __uint_as_float(r[jj]);
                                 } else {
                                     o[jj * ldo] = __uint_as_float(r[jj]);
                                 }
@@ -573,13 +586,16 @@ int sm_count() {
 // K atoms per pipeline stage of a tile configuration (matches launch_kind).
 int k_atoms(int wt, int bt) { return (wt == 128 && bt <= 128) ? 2 : 1; }
 
-// Tile plan.  Cost model, measured on B200: the single MMA-issuing thread is
-// the critical path once data streams from L2/HBM; an M=128 tcgen05.mma takes
-// max(55, N/2) cycles and every stage adds ~150 cycles of barrier wait,
-// commit and loop.  A persistent CTA runs ceil(units / SMs) units of
-// ceil(K atoms / KA) stages; the estimate is the larger of that and the HBM
-// time of the unique bytes.  Ties prefer more units (more SMs streaming).
-// K is split only for long-K shapes that would leave most SMs idle.
+// Tile plan.  Cost model, measured on B200: a stage costs the larger of
+//  - the MMA thread's work: an M=128 tcgen05.mma takes max(55, N/2) cycles
+//    (a 256-row tile issues two per K step, ~15% dearer than one MMA of twice
+//    the N) plus ~150 cycles of barrier wait, commit and loop per stage, and
+//  - the stage's bytes over the L2 -> SM bandwidth when every SM streams,
+//    ~60 bytes per cycle per SM (about 17 TB/s on 148 SMs).
+// A persistent CTA runs ceil(units / SMs) units of ceil(K atoms / KA)
+// stages; the estimate is the larger of that and the HBM time of the unique
+// bytes.  Ties prefer more units (more SMs streaming), then the earlier
+// option.  K is split only for long-K shapes that would leave most SMs idle.
 GemmPlan plan_gemm(int kind, int m, int n, int k) {
     GemmPlan pl;
     const int eb = kind == 0 ? 1 : 2;
@@ -588,7 +604,7 @@ GemmPlan plan_gemm(int kind, int m, int n, int k) {
     struct Opt {
         int wt, bt;
     };
-    static const Opt opts[] = {{256, 128}, {128, 256}, {128, 128}, {256, 64}, {128, 64},
+    static const Opt opts[] = {{128, 256}, {256, 128}, {128, 128}, {256, 64}, {128, 64},
                                {256, 32},  {128, 32},  {256, 16},  {128, 16}};
     const double hbm_us = (static_cast<double>(n) * k * eb + static_cast<double>(m) * k * eb + 4.0 * m * n) / 6.5e6;
     double best = 1e30;
@@ -597,7 +613,9 @@ GemmPlan plan_gemm(int kind, int m, int n, int k) {
         if (o.bt > 16 && o.bt >= 2 * m) continue;  // mostly empty token tiles
         const int ka = k_atoms(o.wt, o.bt);
         const int units = ((n + o.wt - 1) / o.wt) * ((m + o.bt - 1) / o.bt);
-        const double stage_cyc = 4.0 * ka * (o.wt / 128) * std::max(55.0, o.bt / 2.0) + 150.0;
+        const double mma_cyc = 4.0 * ka * (o.wt / 128) * std::max(55.0, o.bt / 2.0) * (o.wt == 256 ? 1.15 : 1.0);
+        const double l2_cyc = ka * (o.wt + o.bt) * static_cast<double>(kKBytes) / 60.0;
+        const double stage_cyc = std::max(mma_cyc + 150.0, l2_cyc);
         const double unit_cyc = ((num_kb + ka - 1) / ka) * stage_cyc;
         const double est = std::max(((units + sms - 1) / sms) * unit_cyc / 1900.0 + 1.0, hbm_us);
         if (est < best * 0.999 || (est < best * 1.001 && units > best_units)) {
@@ -650,8 +668,10 @@ int launch_gemm_tc(int kind, const void* w, long long ldw_bytes, const void* a, 
         (reinterpret_cast<uintptr_t>(a) % 16))
         return cudaErrorInvalidValue;
     const int eb = kind == 0 ? 1 : 2;
+    if (outs.copies < 1 || outs.copies > kMaxCopies || (outs.copies > 1 && outs.count != 1))
+        return cudaErrorInvalidValue;
     GemmPlan pl = plan_gemm(kind, m, n, k);
-    if (pl.ksplit > 1 && (ws == nullptr || ws->ws == nullptr || ws->counters == nullptr ||
+    if (pl.ksplit > 1 && (outs.copies > 1 || ws == nullptr || ws->ws == nullptr || ws->counters == nullptr ||
                           ws->ws_elems < pl.ws_elems || ws->counter_elems < pl.counter_elems)) {
         // no (large enough) workspace: one unit per tile over the whole K
         pl.ksplit = 1;
@@ -667,6 +687,10 @@ int launch_gemm_tc(int kind, const void* w, long long ldw_bytes, const void* a, 
     p.tiles_n = (n + pl.wt - 1) / pl.wt;
     p.tiles_m = (m + pl.bt - 1) / pl.bt;
     p.group_m = std::min(p.tiles_m, 8);
+    if (const char* v = std::getenv("ROCKNPU_B200_GEMM_GROUP")) {
+        const int gm = std::atoi(v);
+        if (gm >= 1) p.group_m = std::min(p.tiles_m, gm);
+    }
     p.ksplit = pl.ksplit;
     p.kb_per_split = pl.kb_per_split;
     p.units = p.tiles_n * p.tiles_m * p.ksplit;
@@ -676,6 +700,8 @@ int launch_gemm_tc(int kind, const void* w, long long ldw_bytes, const void* a, 
         p.out[i] = outs.out[i];
         p.ldo[i] = outs.ldo[i];
     }
+    p.copies = outs.copies;
+    for (int i = 0; i < kMaxCopies; ++i) p.copy_out[i] = i < outs.copies ? outs.copy_out[i] : nullptr;
     p.acc_out = acc_out;
     p.acc_ld = acc_ld;
     p.ws = pl.ksplit > 1 ? ws->ws : nullptr;

@@ -15,13 +15,20 @@ inline size_t qblock_bytes(int kind) {
     return kind == kQ4K ? 144 : kind == kQ5K ? 176 : kind == kQ6K ? 210 : 0;
 }
 
+constexpr int kMaxCopies = 16;  // ranks of one node an output tile can go to
+
 // Up to four output members of one concatenated-N GEMM: member i owns the
 // weight rows [n_start[i], n_start[i+1]) and writes out[i][m * ldo[i] + col].
+// With one member, copies > 1 writes every element to copy_out[0..copies)
+// at the same offset instead (copy 0 is usually out[0]): the all-gather of an
+// N-sharded GEMM over peer memory.  Launches with copies > 1 do not split K.
 struct OutMembers {
     int count = 1;
     int n_start[5] = {0, 0, 0, 0, 0};
     float* out[4] = {nullptr, nullptr, nullptr, nullptr};
     long long ldo[4] = {0, 0, 0, 0};
+    int copies = 1;
+    float* copy_out[kMaxCopies] = {};
 };
 
 // K1: Q4_K/Q5_K/Q6_K rows -> int8 rows [n, k] + per-row scales [n].

@@ -17,6 +17,7 @@ enum DeviceError : int {
     kErrTimeoutEmpty = 3,   // producer: smem stage never released
     kErrTimeoutAccum = 4,   // epilogue: accumulator never completed
     kErrTimeoutDrain = 5,   // teardown: in-flight copies did not drain
+    kErrTimeoutPeer = 6,    // peer barrier: another rank never arrived
 };
 
 // Wait limit of every spin in the library (the reference's NPU completion
