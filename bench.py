@@ -74,6 +74,20 @@ def h2d_d2h_bytes(m: int):
     return h2d, d2h
 
 
+def profiled_traffic(m: int):
+    """DRAM bytes per step of the GEMM launches, from the committed ncu
+    summary of this workload (profiles/gemm_tc_tinyllama_pp512_dram.md);
+    None for token counts that were not captured."""
+    path = os.path.join(ROOT, "profiles", f"gemm_tc_tinyllama_pp{m}_dram.md")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        for line in f:
+            if line.startswith("traffic_bytes_per_step:"):
+                return int(line.split(":")[1])
+    return None
+
+
 def load_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -303,7 +317,9 @@ def run_ours(args, rank: int, world: int):
     else:
         roof = {"bound": "tensor", "achieved": round(tops, 1), "peak": int8_peak_tops, "unit": "TOP/s",
                 "frac": round(tops / int8_peak_tops, 4)}
-    roof.update({"kernel": "gemm_tc_kernel (K3, tcgen05 kind::i8)", "traffic": None,
+    traffic = profiled_traffic(m)
+    roof.update({"kernel": "gemm_tc_kernel (K3, tcgen05 kind::i8)", "traffic": traffic,
+                 "traffic_unit": "DRAM bytes per step (88 launches), ncu capture" if traffic else None,
                  "peak_source": f"{peak_src} (int8 = 2 x bf16_tflops)" if roof["bound"] == "tensor"
                  else f"{peak_src} hbm_gbs",
                  "hbm_frac": round(gb_s / hbm_peak, 4), "tensor_frac": round(tops / int8_peak_tops, 4),
