@@ -11,8 +11,9 @@ in a step.  Weights are random-init (N(0, 0.02^2) encoded to Q4_K/Q6_K),
 activations N(0, 1); prepared int8 weights are resident (the reference's
 weight cache), 1.0 GB per step > L2, so no extra L2 flush is needed.
 
-* value: tok/s with activations already in HBM (device entry points:
-  K2 per-token quantisation + K3 tcgen05 W8A8 GEMM per MUL_MAT).
+* value: tok/s with activations already in HBM (device entry point
+  rocknpu_b200_matmul_w8a8 per MUL_MAT: K2 per-token quantisation + the K3
+  tcgen05 W8A8 GEMM, launched programmatically after it).
 * e2e:   tok/s through the reference C ABI with pinned host buffers, as the
   plugin calls it (rocknpu_matmul_q_concat_f32_f32_mtile for the groups,
   rocknpu_matmul_q{4,6}_k_f32_f32 for O and down): H2D of every activation
@@ -72,6 +73,32 @@ def h2d_d2h_bytes(m: int):
             h2d += 4 * m * k
             d2h += 4 * m * sum(nn for _, nn in members)
     return h2d, d2h
+
+
+def new_graph():
+    import torch
+    try:
+        return torch.cuda.CUDAGraph(keep_graph=True)
+    except TypeError:
+        return torch.cuda.CUDAGraph()
+
+
+def graph_kernel_nodes(graph):
+    """Kernel nodes of a captured CUDA graph (counted, not assumed), or None
+    when the graph cannot be inspected."""
+    try:
+        from cuda.bindings import runtime as rt
+        g = graph.raw_cuda_graph()
+        err, _, count = rt.cudaGraphGetNodes(g, 0)
+        err, nodes, count = rt.cudaGraphGetNodes(g, count)
+        kernels = 0
+        for node in nodes[:count]:
+            err, kind = rt.cudaGraphNodeGetType(node)
+            if kind == rt.cudaGraphNodeType.cudaGraphNodeTypeKernel:
+                kernels += 1
+        return kernels
+    except Exception:
+        return None
 
 
 def profiled_traffic(m: int):
@@ -238,7 +265,6 @@ def run_ours(args, rank: int, world: int):
         for key, (w8, s8, k) in prepared.items():
             dev.matmul_w8a8(ctx, d_acts[key], w8, s8, outs[key[1]])
 
-    launches_per_step = 2 * len(prepared)
 
     dist = None
     if world > 1:
@@ -250,13 +276,14 @@ def run_ours(args, rank: int, world: int):
             dist.barrier()
 
     # eager warm-up sizes the context workspaces, then the step is captured
-    # once as a CUDA graph (176 launches, quantiser -> GEMM edges are
-    # programmatic dependent launches) and replayed
+    # once as a CUDA graph (88 x {K2, K3}, each GEMM a programmatic dependent
+    # launch of its quantiser) and replayed
     step()
     torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
+    graph = new_graph()
     with torch.cuda.graph(graph):
         step()
+    launches_per_step = graph_kernel_nodes(graph)
     for _ in range(args.warmup):
         graph.replay()
     torch.cuda.synchronize()
@@ -397,7 +424,8 @@ def run_ours(args, rank: int, world: int):
         "roofline": roof,
         "e2e": e2e,
         "cpu_baseline": cpu,
-        "gpu_launches": launches_per_step * args.steps,
+        "gpu_launches": launches_per_step * args.steps if launches_per_step is not None else None,
+        "launches_per_step": launches_per_step,
         "clocks": clocks.summary(),
         "setup_s": round(gen_s, 1),
     }

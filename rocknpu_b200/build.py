@@ -24,8 +24,8 @@ LIB = os.path.join(HERE, "librocknpu.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3",
               "--expt-relaxed-constexpr", "-I", INCLUDE]
-SOURCES = ["quant.cu", "gemm.cu", "gemv.cu", "noalloc.cu", "shard.cu", "capi.cpp", "plugin_rules.cpp", "synth.cpp"]
-HEADERS = ["kernels.h", "ptx.cuh"]
+SOURCES = ["quant.cu", "gemm.cu", "gemm_plain.cu", "gemm_fused.cu", "gemm_gather.cu", "gemv.cu", "noalloc.cu", "shard.cu", "capi.cpp", "plugin_rules.cpp", "synth.cpp"]
+HEADERS = ["kernels.h", "ptx.cuh", "quant_math.cuh", "gemm_kernel.cuh"]
 
 
 def nvcc() -> str:
@@ -52,7 +52,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
         if force or not os.path.exists(o) or os.path.getmtime(o) < max(os.path.getmtime(s), hdr):
             lang = [] if src.endswith(".cu") else ["-x", "cu"] if src in ("capi.cpp",) else []
             cmd = [nvcc(), *ARCH, *NVCC_FLAGS, *lang, "-c", s, "-o", o]
-            if src == "gemm.cu":
+            if src.startswith("gemm_"):
                 cmd += ["-Xptxas", "-v"] if verbose else []
             jobs.append(cmd)
     if jobs:

@@ -243,7 +243,8 @@ struct RockNpuContext {
     int* h_status = nullptr;  // pinned mirror
 
     DevBuf a_f32, a_i8, a_scale, a_f16, out_f32, staging, swiglu_tmp;
-    DevBuf gemm_ws;  // split-K workspace, all-zero between launches
+    DevBuf gemm_ws;      // split-K workspace, all-zero between launches
+    DevBuf quant_sync;   // fused-quantiser counters, all-zero between launches
 
     // Prompt-path (M-tile) resident weights: single projections and
     // concatenated same-input groups (L:1808-1849, L:2351-2384).
@@ -286,6 +287,7 @@ int finish(Ctx* c) {
     if (s == rk::kErrNone) return kOk;
     // a launch that stopped early may leave split-K partials behind
     if (s != rk::kErrNonFinite && c->gemm_ws.ptr) cudaMemset(c->gemm_ws.ptr, 0, c->gemm_ws.cap);
+    if (s != rk::kErrNonFinite && c->quant_sync.ptr) cudaMemset(c->quant_sync.ptr, 0, c->quant_sync.cap);
     cudaMemset(c->d_status, 0, sizeof(int));
     return s == rk::kErrNonFinite ? kInvalid : kExecError;
 }
@@ -302,6 +304,33 @@ int context_ws(Ctx* c, size_t m, size_t n, size_t k, rk::GemmWorkspace* out) {
 }
 
 int reset_status(Ctx* c) { return cuda_status(cudaMemsetAsync(c->d_status, 0, sizeof(int), c->stream)); }
+
+// K2 + K3 over activation rows already in HBM: the quantiser runs fused into
+// the GEMM's prologue when that pays (rk::fused_quant_enabled), else as its
+// own launch.  Returns a cudaError_t value.
+int launch_w8a8(Ctx* c, const int8_t* w, const float* w_scales, const float* a_dev, size_t m, size_t k, size_t n,
+                int8_t* a8, size_t ld8, float* as, const rk::OutMembers& om, const rk::GemmWorkspace* gws,
+                cudaStream_t s) {
+    const int mi = static_cast<int>(m), ki = static_cast<int>(k), ni = static_cast<int>(n);
+    if (rk::fused_quant_enabled(mi, ki) && reinterpret_cast<uintptr_t>(a_dev) % 16 == 0) {
+        const size_t elems = rk::fused_quant_sync_elems(mi, ni, ki);
+        if (c->quant_sync.ensure(elems * sizeof(unsigned)) != cudaSuccess) return cudaErrorMemoryAllocation;
+        rk::FusedQuant fq;
+        fq.a = a_dev;
+        fq.lda = static_cast<long long>(k);
+        fq.a8 = a8;
+        fq.ld8 = static_cast<long long>(ld8);
+        fq.scales = as;
+        fq.sync = c->quant_sync.as<unsigned>();
+        fq.sync_elems = c->quant_sync.cap / sizeof(unsigned);
+        return rk::launch_gemm_tc(0, w, static_cast<long long>(k), a8, static_cast<long long>(ld8), mi, ni, ki,
+                                  w_scales, as, om, nullptr, 0, c->d_status, s, gws, &fq);
+    }
+    rk::launch_quant_rows(a_dev, mi, ki, static_cast<long long>(k), a8, static_cast<long long>(ld8), as, c->d_status,
+                          s);
+    return rk::launch_gemm_tc(0, w, static_cast<long long>(k), a8, static_cast<long long>(ld8), mi, ni, ki, w_scales,
+                              as, om, nullptr, 0, c->d_status, s, gws);
+}
 
 // Dequantise + requantise host K-quant rows into w/scales (device), rows of
 // one member of a (possibly concatenated) prepared weight.
@@ -434,8 +463,6 @@ int run_w8a8(Ctx* c, const PreparedW8& pw, const float* host_a, size_t m, size_t
         if (cudaMemcpyAsync(a_dev + r0 * k, host_a + r0 * k, mr * k * sizeof(float), cudaMemcpyHostToDevice, c->h2d) ||
             cudaEventRecord(ein, c->h2d) || cudaStreamWaitEvent(c->stream, ein, 0))
             return kExecError;
-        rk::launch_quant_rows(a_dev + r0 * k, static_cast<int>(mr), static_cast<int>(k), static_cast<long long>(k),
-                              a8 + r0 * ld8, static_cast<long long>(ld8), as + r0, c->d_status, c->stream);
         rk::OutMembers om;
         om.count = static_cast<int>(nseg);
         size_t start = 0;
@@ -446,10 +473,8 @@ int run_w8a8(Ctx* c, const PreparedW8& pw, const float* host_a, size_t m, size_t
             start += segs[i].n;
         }
         om.n_start[nseg] = static_cast<int>(start);
-        const int e = rk::launch_gemm_tc(0, pw.w, static_cast<long long>(pw.k), a8 + r0 * ld8,
-                                         static_cast<long long>(ld8), static_cast<int>(mr), static_cast<int>(total_n),
-                                         static_cast<int>(k), pw.scales, as + r0, om, nullptr, 0, c->d_status,
-                                         c->stream, &gws);
+        const int e = launch_w8a8(c, pw.w, pw.scales, a_dev + r0 * k, mr, k, total_n, a8 + r0 * ld8, ld8, as + r0, om,
+                                  &gws, c->stream);
         if (e != cudaSuccess || cudaEventRecord(eout, c->stream) || cudaStreamWaitEvent(c->d2h, eout, 0))
             return kExecError;
         if (rows >= m) {
@@ -725,6 +750,7 @@ rocknpu_context* rocknpu_context_create(void) {
     c->direct_submit = std::getenv("ROCKNPU_W8_DIRECT_SUBMIT") != nullptr;
     c->profile = env_enabled("ROCKNPU_MTILE_PROFILE");
     c->gemm_ws.zeroed = true;
+    c->quant_sync.zeroed = true;
     bool events_ok = true;
     for (int i = 0; i < RockNpuContext::kMaxChunks && events_ok; ++i)
         events_ok = cudaEventCreateWithFlags(&c->ev_in[i], cudaEventDisableTiming) == cudaSuccess &&
@@ -780,7 +806,7 @@ void rocknpu_context_destroy(rocknpu_context* context) {
     c->decode_groups.clear();
     c->f16.clear();
     for (DevBuf* b : {&c->a_f32, &c->a_i8, &c->a_scale, &c->a_f16, &c->out_f32, &c->staging, &c->swiglu_tmp,
-                      &c->gemm_ws})
+                      &c->gemm_ws, &c->quant_sync})
         b->release();
     if (c->d_status) cudaFree(c->d_status);
     if (c->h_status) cudaFreeHost(c->h_status);
@@ -1138,10 +1164,9 @@ int rocknpu_b200_matmul_w8a8(rocknpu_context* context, const float* a, const int
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : context->stream;
     const size_t ld8 = round_up(k, 16);
     if (context->a_i8.ensure(m * ld8) || context->a_scale.ensure(m * sizeof(float))) return kExecError;
-    rk::launch_quant_rows(a, static_cast<int>(m), static_cast<int>(k), static_cast<long long>(k),
-                          context->a_i8.as<int8_t>(), static_cast<long long>(ld8), context->a_scale.as<float>(),
-                          context->d_status, s);
     if (m == 1 && k % 16 == 0) {
+        rk::launch_quant_rows(a, 1, static_cast<int>(k), static_cast<long long>(k), context->a_i8.as<int8_t>(),
+                              static_cast<long long>(ld8), context->a_scale.as<float>(), context->d_status, s);
         rk::launch_gemv_w8a8(w_i8, w_scales, context->a_i8.as<int8_t>(), context->a_scale.as<float>(),
                              static_cast<int>(k), static_cast<int>(n), out, s);
         return cuda_status(cudaGetLastError());
@@ -1153,9 +1178,8 @@ int rocknpu_b200_matmul_w8a8(rocknpu_context* context, const float* a, const int
     om.n_start[1] = static_cast<int>(n);
     om.out[0] = out;
     om.ldo[0] = static_cast<long long>(n);
-    const int e = rk::launch_gemm_tc(0, w_i8, static_cast<long long>(k), context->a_i8.ptr, static_cast<long long>(ld8),
-                                     static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), w_scales,
-                                     context->a_scale.as<float>(), om, nullptr, 0, context->d_status, s, &gws);
+    const int e = launch_w8a8(context, w_i8, w_scales, a, m, k, n, context->a_i8.as<int8_t>(), ld8,
+                              context->a_scale.as<float>(), om, &gws, s);
     return e == cudaSuccess ? kOk : kExecError;
 }
 

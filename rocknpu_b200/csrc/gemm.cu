@@ -48,441 +48,13 @@
 #include <cstdlib>
 #include <mutex>
 
-#include "kernels.h"
-#include "ptx.cuh"
+#include "gemm_kernel.cuh"
 
 namespace rk {
 namespace {
 
-constexpr int kKBytes = 128;  // K bytes per stage (one swizzle row)
-constexpr int kEpiWarps = 8;
-constexpr int kThreads = (3 + kEpiWarps) * 32;
-
-struct GemmParams {
-    CUtensorMap tmap_w;  // [n rows][k] K-major, box WT rows
-    CUtensorMap tmap_a;  // [m rows][k] K-major, box BT rows
-    const float* w_scale;
-    const float* a_scale;
-    int m, n, num_kb, kb_elems;
-    int tiles_n, tiles_m, group_m;
-    int units, ksplit, kb_per_split;
-    int nmembers;
-    int n_start[5];
-    float* out[4];
-    long long ldo[4];
-    int copies;                   // > 1: elements go to every copy_out[c] instead
-    float* copy_out[kMaxCopies];  // at out[0]'s offsets (peer all-gather)
-    int32_t* acc_out;
-    long long acc_ld;
-    int32_t* ws;         // split-K partial sums [m][n], all zero between launches
-    unsigned* counters;  // split-K arrivals per tile, all zero between launches
-    int* err;
-};
-
-template <int WT, int BT, int KA, int STAGES>
-struct Cfg {
-    static constexpr int kAcc = WT / 128;  // accumulators per tile
-    static constexpr int kWBox = WT * kKBytes;  // one K atom of the weight tile
-    static constexpr int kABox = BT * kKBytes;  // one K atom of the token tile
-    static constexpr int kWBytes = KA * kWBox;
-    static constexpr int kABytes = KA * kABox;
-    static constexpr int kStage = kWBytes + kABytes;
-    static constexpr int kBarOffset = STAGES * kStage;
-    static constexpr int kNumBars = 2 * STAGES + 5;
-    static constexpr int kBytes = kBarOffset + kNumBars * 8 + 32 + 1024;  // + alignment slack
-    static constexpr uint32_t kTmemCols = 2 * kAcc * BT < 32 ? 32 : 2 * kAcc * BT;
-    static_assert((kTmemCols & (kTmemCols - 1)) == 0 && kTmemCols <= 512, "TMEM allocation");
-    static_assert(kBytes <= 232448, "shared memory");
-};
-
-struct Shared {
-    uint64_t* full;  // two arrivals per phase: weight and activation producer
-    uint64_t* empty;
-    uint64_t* tfull;   // [2]
-    uint64_t* tempty;  // [2]
-    uint64_t* drain;
-    uint32_t* tmem_slot;
-    uint32_t* last_flag;
-    volatile uint32_t* abort;
-};
-
-__device__ __forceinline__ void fail(const GemmParams& p, const Shared& sh, int code) {
-    atomicCAS(p.err, 0, code);
-    *sh.abort = 1u;
-}
-
-// Bounded wait that also gives up once another role has aborted.
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile uint32_t* abort) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = globaltimer_ns();
-    while (true) {
-#pragma unroll 1
-        for (int i = 0; i < 32; ++i)
-            if (mbar_try_wait(bar, parity)) return true;
-        if (*abort) return false;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
-    }
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-
-__device__ __forceinline__ void epilogue_bar() {
-    asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
-}
-
-__device__ __forceinline__ int member_of(const GemmParams& p, int col) {
-    int mi = 0;
-#pragma unroll
-    for (int i = 1; i < 4; ++i)
-        if (i < p.nmembers && col >= p.n_start[i]) mi = i;
-    return mi;
-}
-
-// Unit u -> tile coordinates and K range.  Grouped rasterisation: group_m
-// token tiles advance together so a wave's weight and activation tiles stay
-// L2-resident.
-struct Unit {
-    int tile, n0, m0, kb0, kb1;
-};
-
-template <int WT, int BT>
-__device__ __forceinline__ Unit unit_coords(const GemmParams& p, int u) {
-    Unit r;
-    r.tile = u / p.ksplit;
-    const int split = u - r.tile * p.ksplit;
-    const int per_group = p.group_m * p.tiles_n;
-    const int g = r.tile / per_group;
-    const int first_m = g * p.group_m;
-    const int gsz = min(p.group_m, p.tiles_m - first_m);
-    const int local = r.tile - g * per_group;
-    r.m0 = (first_m + local % gsz) * BT;
-    r.n0 = (local / gsz) * WT;
-    r.kb0 = split * p.kb_per_split;
-    r.kb1 = min(p.num_kb, r.kb0 + p.kb_per_split);
-    return r;
-}
-
-// Last unit of a split-K tile: read the summed int32 tile from the
-// workspace (vector loads, several rows in flight per thread), rescale,
-// write the outputs, and return the cells and the tile counter to zero.
-template <int WT, int BT>
-__device__ __forceinline__ void finalize_split(const GemmParams& p, const Unit& u, int tid, bool leader) {
-    constexpr int kGroups = WT / 4;                       // 4-column groups per tile
-    constexpr int kRowStep = (kEpiWarps * 32) / kGroups;  // rows handled in parallel
-    const long long wld = p.n;
-    const int mend = min(p.m, u.m0 + BT);
-    const int c0 = u.n0 + (tid % kGroups) * 4;
-    const int r0 = u.m0 + tid / kGroups;
-    if ((p.n & 3) == 0) {
-        if (c0 < p.n) {
-            float wsc[4];
-            float* optr[4];
-            long long oldo[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int col = c0 + j;
-                wsc[j] = p.w_scale[col];
-                const int mi = member_of(p, col);
-                optr[j] = p.out[mi] + (col - p.n_start[mi]);
-                oldo[j] = p.ldo[mi];
-            }
-            for (int rb = r0; rb < mend; rb += 4 * kRowStep) {
-                int4 v[4];
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const int m = rb + t * kRowStep;
-                    if (m < mend) v[t] = __ldcg(reinterpret_cast<const int4*>(p.ws + m * wld + c0));
-                }
-                float a_sv[4];
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const int m = rb + t * kRowStep;
-                    a_sv[t] = m < mend ? __ldg(p.a_scale + m) : 0.0f;
-                }
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const int m = rb + t * kRowStep;
-                    if (m < mend) {
-                        *reinterpret_cast<int4*>(p.ws + m * wld + c0) = make_int4(0, 0, 0, 0);
-                        const float a_s = a_sv[t];
-                        const int acc[4] = {v[t].x, v[t].y, v[t].z, v[t].w};
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            optr[j][m * oldo[j]] = __fmul_rn(__fmul_rn(__int2float_rn(acc[j]), a_s), wsc[j]);
-                            if (p.acc_out) p.acc_out[m * p.acc_ld + c0 + j] = acc[j];
-                        }
-                    }
-                }
-            }
-        }
-    } else {
-        // odd widths: one cell per thread per step
-        for (int idx = tid; idx < WT * BT; idx += kEpiWarps * 32) {
-            const int col = u.n0 + idx % WT;
-            const int m = u.m0 + idx / WT;
-            if (col < p.n && m < mend) {
-                const int mi = member_of(p, col);
-                int32_t* cell = p.ws + m * wld + col;
-                const int acc = __ldcg(cell);
-                *cell = 0;
-                p.out[mi][m * p.ldo[mi] + (col - p.n_start[mi])] =
-                    __fmul_rn(__fmul_rn(__int2float_rn(acc), p.a_scale[m]), p.w_scale[col]);
-                if (p.acc_out) p.acc_out[m * p.acc_ld + col] = acc;
-            }
-        }
-    }
-    if (leader) p.counters[u.tile] = 0u;
-}
-
-template <int KIND, int WT, int BT, int KA, int STAGES>
-__global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ GemmParams p) {
-    using C = Cfg<WT, BT, KA, STAGES>;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
-    Shared sh;
-    sh.full = bars;
-    sh.empty = bars + STAGES;
-    sh.tfull = bars + 2 * STAGES;
-    sh.tempty = sh.tfull + 2;
-    sh.drain = sh.tempty + 2;
-    sh.tmem_slot = reinterpret_cast<uint32_t*>(sh.drain + 1);
-    sh.last_flag = sh.tmem_slot + 1;
-    sh.abort = sh.tmem_slot + 2;
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&sh.full[s], 2);
-            mbar_init(&sh.empty[s], 1);
-        }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&sh.tfull[b], 1);
-            mbar_init(&sh.tempty[b], kEpiWarps);
-        }
-        mbar_init(sh.drain, 1);
-        *sh.abort = 0u;
-        fence_mbar_init();
-        prefetch_tmap(&p.tmap_w);
-        prefetch_tmap(&p.tmap_a);
-    }
-    if (warp == 2) {
-        tmem_alloc(sh.tmem_slot, C::kTmemCols);
-        tmem_relinquish();
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem_base = *sh.tmem_slot;
-
-    if (warp == 0 || warp == 1) {
-        if (lane == 0) {
-            // ---- producers: warp 0 weights, warp 1 activations ----
-            const bool is_w = warp == 0;
-            const CUtensorMap* map = is_w ? &p.tmap_w : &p.tmap_a;
-            const uint32_t box = is_w ? C::kWBox : C::kABox;
-            const int off = is_w ? 0 : C::kWBytes;
-            if (!is_w) griddep_wait();
-            int g = 0;
-            bool ok = true;
-            for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
-                const Unit t = unit_coords<WT, BT>(p, u);
-                const int row = is_w ? t.n0 : t.m0;
-                for (int kb = t.kb0; kb < t.kb1; kb += KA, ++g) {
-                    const int s = g % STAGES;
-                    const uint32_t ph = (g / STAGES) & 1;
-                    if (g >= STAGES && !wait_or_abort(&sh.empty[s], ph ^ 1, sh.abort)) {
-                        if (!*sh.abort) fail(p, sh, kErrTimeoutEmpty);
-                        ok = false;
-                        break;
-                    }
-                    const int na = min(KA, t.kb1 - kb);  // K atoms in this stage
-                    mbar_arrive_expect_tx(&sh.full[s], na * box);
-                    for (int a = 0; a < na; ++a)
-                        tma_load_2d(smem + s * C::kStage + off + a * box, map, &sh.full[s], (kb + a) * p.kb_elems, row);
-                }
-            }
-            // our copies in flight must land before the CTA exits: wait for
-            // the stage's phase, or give up after the limit (the other
-            // producer's arrival is part of the phase)
-            for (int i = max(0, g - STAGES); i < g; ++i) {
-                if (!mbar_wait(&sh.full[i % STAGES], (i / STAGES) & 1)) {
-                    atomicCAS(p.err, 0, kErrTimeoutDrain);
-                    break;
-                }
-            }
-        }
-    } else if (warp == 2) {
-        if (lane == 0) {
-            // ---- MMA issuer ----
-            constexpr uint32_t idesc = make_idesc<KIND>(128, BT);
-            int g = 0, j = 0;
-            bool ok = true;
-            for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x, ++j) {
-                const Unit t = unit_coords<WT, BT>(p, u);
-                const int buf = j & 1, use = j >> 1;
-                if (use >= 1 && !wait_or_abort(&sh.tempty[buf], (use - 1) & 1, sh.abort)) {
-                    if (!*sh.abort) fail(p, sh, kErrTimeoutAccum);
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t d0 = tmem_base + static_cast<uint32_t>(buf * C::kAcc * BT);
-                for (int kb = t.kb0; kb < t.kb1; kb += KA, ++g) {
-                    const int s = g % STAGES;
-                    const uint32_t ph = (g / STAGES) & 1;
-                    if (!wait_or_abort(&sh.full[s], ph, sh.abort)) {
-                        if (!*sh.abort) fail(p, sh, kErrTimeoutFull);
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const int na = min(KA, t.kb1 - kb);
-                    const uint32_t wa = smem_u32(smem + s * C::kStage);
-                    const uint32_t aa = wa + C::kWBytes;
-#pragma unroll
-                    for (int a = 0; a < KA; ++a) {
-                        if (a < na) {
-#pragma unroll
-                            for (int ks = 0; ks < kKBytes / 32; ++ks) {
-#pragma unroll
-                                for (int acc = 0; acc < C::kAcc; ++acc)
-                                    tc_mma<KIND>(d0 + acc * BT,
-                                                 smem_desc_k128(wa + a * C::kWBox + acc * 128 * kKBytes + ks * 32),
-                                                 smem_desc_k128(aa + a * C::kABox + ks * 32), idesc,
-                                                 (kb != t.kb0 || a != 0 || ks != 0) ? 1u : 0u);
-                            }
-                        }
-                    }
-                    tc_commit(&sh.empty[s]);
-                }
-                if (ok) tc_commit(&sh.tfull[buf]);
-            }
-            // our MMAs must finish before TMEM is released
-            tc_commit(sh.drain);
-            if (!mbar_wait(sh.drain, 0)) atomicCAS(p.err, 0, kErrTimeoutDrain);
-        }
-        __syncwarp();
-    } else {
-        // ---- epilogue warps 3..10 ----
-        const int e = warp - 3;
-        const int q = warp & 3;   // TMEM lane quarter this warp may access
-        const int half = e >> 2;  // 0 or 1
-        const int etid = threadIdx.x - 96;
-        bool waited_dep = false;
-        int j = 0;
-        for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++j) {
-            const Unit t = unit_coords<WT, BT>(p, u);
-            const int buf = j & 1, use = j >> 1;
-            int ready = 0;
-            if (lane == 0) ready = wait_or_abort(&sh.tfull[buf], use & 1, sh.abort) ? 1 : 0;
-            ready = __shfl_sync(0xffffffffu, ready, 0);
-            if (!ready && lane == 0 && !*sh.abort) fail(p, sh, kErrTimeoutAccum);
-            if (!waited_dep) {
-                griddep_wait();
-                waited_dep = true;
-            }
-            // accumulator and output column this thread handles
-            const int acc = C::kAcc == 2 ? half : 0;
-            const int col = t.n0 + acc * 128 + q * 32 + lane;
-            const bool col_ok = col < p.n;
-            const int mi = member_of(p, col);
-            float* out = p.out[mi];
-            const long long ldo = p.ldo[mi];
-            const int ocol = col - p.n_start[mi];
-            float wsc = 0.0f;
-            if constexpr (KIND == 0) wsc = col_ok ? p.w_scale[col] : 0.0f;
-            const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                                       static_cast<uint32_t>((buf * C::kAcc + acc) * BT);
-            // with one accumulator the two halves split the token columns
-            const int c_first = C::kAcc == 2 ? 0 : half * 16;
-            const int c_step = C::kAcc == 2 ? 16 : 32;
-            const bool split = KIND == 0 && p.ksplit > 1;
-            if (ready) {
-                tc_fence_after();
-                const float* __restrict__ a_scale = p.a_scale;
-                int32_t* __restrict__ acc_out = p.acc_out;
-                int32_t* __restrict__ wsp = p.ws;
-#pragma unroll 1
-                for (int c = c_first; c < BT; c += c_step) {
-                    // the chunk's token scales, loaded before any store of
-                    // the chunk (stores could otherwise order every load)
-                    float asv[16];
-                    if constexpr (KIND == 0) {
-#pragma unroll
-                        for (int jj = 0; jj < 16; ++jj) {
-                            const int m = t.m0 + c + jj;
-                            asv[jj] = (!split && m < p.m) ? __ldg(a_scale + m) : 0.0f;
-                        }
-                    }
-                    uint32_t r[16];
-                    tmem_ld16(lane_base + c, r);
-                    tmem_ld_wait();
-                    if (col_ok) {
-                        float* __restrict__ o = out + static_cast<long long>(t.m0 + c) * ldo + ocol;
-#pragma unroll
-                        for (int jj = 0; jj < 16; ++jj) {
-                            const int m = t.m0 + c + jj;
-                            if (m < p.m) {
-                                if constexpr (KIND == 0) {
-                                    if (split) {
-                                        atomicAdd(wsp + static_cast<long long>(m) * p.n + col, static_cast<int>(r[jj]));
-                                    } else {
-                                        const float v =
-                                            __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[jj])), asv[jj]), wsc);
-                                        if (p.copies > 1) {
-                                            const long long off = static_cast<long long>(m) * ldo + ocol;
-#pragma unroll 1
-                                            for (int cp = 0; cp < p.copies; ++cp) p.copy_out[cp][off] = v;
-                                        } else {
-                                            o[jj * ldo] = v;
-                                        }
-                                        if (acc_out) acc_out[static_cast<long long>(m) * p.acc_ld + col] = r[jj];
-                                    }
-                                } else if (p.copies > 1) {
-                                    const long long off = static_cast<long long>(m) * ldo + ocol;
-#pragma unroll 1
-                                    for (int cp = 0; cp < p.copies; ++cp) p.copy_out[cp][off] = __uint_as_float(r[jj]);
-                                } else {
-                                    o[jj * ldo] = __uint_as_float(r[jj]);
-                                }
-                            }
-                        }
-                    }
-                }
-            }
-            // the TMEM buffer is free for the next unit's MMAs
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&sh.tempty[buf]);
-            if (split) {
-                __threadfence();
-                epilogue_bar();
-                if (etid == 0) {
-                    const unsigned prev = atomicAdd(p.counters + t.tile, 1u);
-                    *sh.last_flag = (prev == static_cast<unsigned>(p.ksplit - 1)) ? 1u : 0u;
-                }
-                epilogue_bar();
-                if (*sh.last_flag) {
-                    __threadfence();
-                    finalize_split<WT, BT>(p, t, etid, etid == 0);
-                }
-            }
-        }
-    }
-
-    __syncwarp();
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 2) {
-        tc_fence_after();
-        tmem_dealloc(tmem_base, C::kTmemCols);
-    }
-}
+using gemm_detail::GemmParams;
+using gemm_detail::kKBytes;
 
 // ---- host side -----------------------------------------------------------
 
@@ -523,52 +95,6 @@ int current_device() {
     return d;
 }
 
-template <int KIND, int WT, int BT, int KA, int STAGES>
-int launch_cfg(GemmParams& p, int grid, cudaStream_t s) {
-    using C = Cfg<WT, BT, KA, STAGES>;
-    auto kern = gemm_tc_kernel<KIND, WT, BT, KA, STAGES>;
-    static bool attr_done[64] = {};
-    const int dev = current_device();
-    if (dev < 0 || dev >= 64 || !attr_done[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kBytes);
-        if (e != cudaSuccess) return e;
-        if (dev >= 0 && dev < 64) attr_done[dev] = true;
-    }
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = C::kBytes;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, p);
-}
-
-// The instantiated tile configurations: (WT, BT, K atoms per stage,
-// stages), each about 200 KB of shared memory.
-template <int KIND>
-int launch_kind(const GemmPlan& pl, GemmParams& p, cudaStream_t s) {
-    const int grid = std::min(p.units, sm_count());
-    if (pl.wt == 256) {
-        switch (pl.bt) {
-            case 16: return launch_cfg<KIND, 256, 16, 1, 6>(p, grid, s);
-            case 32: return launch_cfg<KIND, 256, 32, 1, 5>(p, grid, s);
-            case 64: return launch_cfg<KIND, 256, 64, 1, 5>(p, grid, s);
-            default: return launch_cfg<KIND, 256, 128, 1, 4>(p, grid, s);
-        }
-    }
-    switch (pl.bt) {
-        case 16: return launch_cfg<KIND, 128, 16, 2, 5>(p, grid, s);
-        case 32: return launch_cfg<KIND, 128, 32, 2, 5>(p, grid, s);
-        case 64: return launch_cfg<KIND, 128, 64, 2, 4>(p, grid, s);
-        case 128: return launch_cfg<KIND, 128, 128, 2, 3>(p, grid, s);
-        default: return launch_cfg<KIND, 128, 256, 1, 4>(p, grid, s);
-    }
-}
-
 }  // namespace
 
 int sm_count() {
@@ -583,7 +109,8 @@ int sm_count() {
     return count[dev];
 }
 
-// K atoms per pipeline stage of a tile configuration (matches launch_kind).
+// K atoms per pipeline stage of a tile configuration (matches launch_kind in
+// gemm_kernel.cuh).
 int k_atoms(int wt, int bt) { return (wt == 128 && bt <= 128) ? 2 : 1; }
 
 // Tile plan.  Cost model, measured on B200: a stage costs the larger of
@@ -660,9 +187,28 @@ GemmPlan plan_gemm(int kind, int m, int n, int k) {
     return pl;
 }
 
+size_t fused_quant_sync_elems(int m, int n, int k) {
+    const GemmPlan pl = plan_gemm(0, m, n, k);
+    return static_cast<size_t>((m + pl.bt - 1) / pl.bt) + 1;
+}
+
+bool fused_quant_enabled(int m, int k) {
+    // a row must fit the quantiser's 8 epilogue warps (16384 floats) in
+    // 16-byte vectors
+    if (k % 16 != 0 || k > 8 * gemm_detail::kQuantSeg) return false;
+    // Off unless ROCKNPU_B200_FUSED_QUANT=1.  Measured on B200 (TinyLlama
+    // pp512 calls replayed in a CUDA graph): the standalone quantiser, which
+    // triggers the GEMM's programmatic launch at its start, costs ~4 us per
+    // call; in the prologue the same rows take ~8 us, because only the 8
+    // epilogue warps per SM work on them (latency-bound at that occupancy)
+    // and they can start only once the previous launch has fully drained.
+    const char* v = std::getenv("ROCKNPU_B200_FUSED_QUANT");
+    return v != nullptr && v[0] == '1' && static_cast<long long>(m) * k <= (8ll << 20);
+}
+
 int launch_gemm_tc(int kind, const void* w, long long ldw_bytes, const void* a, long long lda_bytes, int m, int n,
                    int k, const float* w_scale, const float* a_scale, const OutMembers& outs, int32_t* acc_out,
-                   long long acc_ld, int* err, cudaStream_t s, const GemmWorkspace* ws) {
+                   long long acc_ld, int* err, cudaStream_t s, const GemmWorkspace* ws, const FusedQuant* fq) {
     if (m <= 0 || n <= 0 || k <= 0) return cudaErrorInvalidValue;
     if ((ldw_bytes % 16) || (lda_bytes % 16) || (reinterpret_cast<uintptr_t>(w) % 16) ||
         (reinterpret_cast<uintptr_t>(a) % 16))
@@ -707,9 +253,27 @@ int launch_gemm_tc(int kind, const void* w, long long ldw_bytes, const void* a, 
     p.ws = pl.ksplit > 1 ? ws->ws : nullptr;
     p.counters = pl.ksplit > 1 ? ws->counters : nullptr;
     p.err = err;
+    if (fq) {
+        const long long k16 = (k + 15) & ~15;
+        if (kind != 0 || outs.copies > 1 || !fq->a || !fq->a8 || !fq->scales || !fq->sync || fq->ld8 % 16 ||
+            fq->ld8 < k16 || fq->lda < k || fq->lda % 4 || k % 16 || k > 8 * gemm_detail::kQuantSeg ||
+            (reinterpret_cast<uintptr_t>(fq->a) % 16) || (reinterpret_cast<uintptr_t>(fq->a8) % 16) ||
+            a != fq->a8 || a_scale != fq->scales || fq->sync_elems < static_cast<size_t>(p.tiles_m) + 1)
+            return cudaErrorInvalidValue;
+        p.q_a = fq->a;
+        p.q_lda = fq->lda;
+        p.q_k = k;
+        p.q_a8 = fq->a8;
+        p.q_ld8 = fq->ld8;
+        p.q_scale = fq->scales;
+        p.q_ready = fq->sync;
+        p.q_exit = fq->sync + p.tiles_m;
+    }
     if (!make_map(&p.tmap_w, w, eb, k, n, ldw_bytes, pl.wt)) return cudaErrorInvalidValue;
     if (!make_map(&p.tmap_a, a, eb, k, m, lda_bytes, pl.bt)) return cudaErrorInvalidValue;
-    return kind == 0 ? launch_kind<0>(pl, p, s) : launch_kind<1>(pl, p, s);
+    if (fq) return gemm_detail::launch_fused(pl, p, s);
+    if (outs.copies > 1) return kind == 0 ? gemm_detail::launch_gather(pl, p, s) : cudaErrorInvalidValue;
+    return gemm_detail::launch_plain(kind, pl, p, s);
 }
 
 }  // namespace rk

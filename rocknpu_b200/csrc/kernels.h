@@ -52,6 +52,28 @@ struct GemmWorkspace {
     size_t ws_elems = 0, counter_elems = 0;
 };
 
+// Per-token quantisation fused into the W8A8 GEMM (K2 in K3's prologue): the
+// GEMM's epilogue warps quantise the f32 rows a[m][lda] into a8[m][ld8] +
+// scales[m] (ld8 a multiple of 16, a8 16-byte aligned) before their first
+// tile, and the activation producer waits per token tile until its rows are
+// published.  `sync` holds fused_quant_sync_elems() counters, all zero
+// between launches (every launch leaves them zero).  Every CTA of the launch
+// must become resident within the 2 s wait limit (true unless another
+// long-running kernel holds the GPU's SMs).
+struct FusedQuant {
+    const float* a = nullptr;
+    long long lda = 0;
+    int8_t* a8 = nullptr;
+    long long ld8 = 0;
+    float* scales = nullptr;
+    unsigned* sync = nullptr;
+    size_t sync_elems = 0;
+};
+size_t fused_quant_sync_elems(int m, int n, int k);
+// Whether to fuse for this shape: only with ROCKNPU_B200_FUSED_QUANT=1, for
+// activation matrices up to 8 Mi values with k % 16 == 0 and k <= 16384.
+bool fused_quant_enabled(int m, int k);
+
 // Tile plan of one GEMM launch: weight tile rows, token tile height, K
 // splits and the workspace a split launch needs.
 struct GemmPlan {
@@ -66,9 +88,12 @@ GemmPlan plan_gemm(int kind, int m, int n, int k);
 // (multiples of 16).  acc_out (kind 0, optional) receives the raw int32.
 // Returns a cudaError_t value.
 // A null or too small `ws` runs the launch without K splits.
+// With `fq` (kind 0 only) the launch quantises the activations itself: `a`
+// must be fq->a8 and `a_scale` fq->scales.
 int launch_gemm_tc(int kind, const void* w, long long ldw_bytes, const void* a, long long lda_bytes, int m, int n,
                    int k, const float* w_scale, const float* a_scale, const OutMembers& outs, int32_t* acc_out,
-                   long long acc_ld, int* err, cudaStream_t s, const GemmWorkspace* ws = nullptr);
+                   long long acc_ld, int* err, cudaStream_t s, const GemmWorkspace* ws = nullptr,
+                   const FusedQuant* fq = nullptr);
 
 // K5: M=1 W8A8 GEMV over resident int8 rows.
 void launch_gemv_w8a8(const int8_t* w, const float* w_scale, const int8_t* a8, const float* a_scale, int k, int n,

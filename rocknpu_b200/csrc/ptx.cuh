@@ -18,6 +18,7 @@ enum DeviceError : int {
     kErrTimeoutAccum = 4,   // epilogue: accumulator never completed
     kErrTimeoutDrain = 5,   // teardown: in-flight copies did not drain
     kErrTimeoutPeer = 6,    // peer barrier: another rank never arrived
+    kErrTimeoutQuant = 7,   // GEMM with fused quantiser: token rows never published
 };
 
 // Wait limit of every spin in the library (the reference's NPU completion

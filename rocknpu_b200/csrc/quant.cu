@@ -3,14 +3,16 @@
 // Both are HBM-bound byte/float streams: one CTA per row, coalesced vector
 // loads, the dequantised (or loaded) row staged once in shared memory, a
 // block-wide absmax, then 16-byte int8 stores.  Arithmetic follows the
-// reference exactly (no contraction, IEEE division, round half away from
-// zero), so the int8 values are bit-identical to its CPU path.
+// reference exactly (no contraction; the rounding of the IEEE quotient,
+// half away from zero, decided by the certified test in quant_math.cuh), so
+// the int8 values are bit-identical to its CPU path.
 #include <cuda_fp16.h>
 
 #include <algorithm>
 
 #include "kernels.h"
 #include "ptx.cuh"
+#include "quant_math.cuh"
 
 namespace rk {
 namespace {
@@ -110,23 +112,15 @@ __device__ __forceinline__ float block_max(float v, float* red) {
     return red[32];
 }
 
-// quantize_symmetric_into's per-value step (capi/src/lib.rs:650-652):
-// round_half_away(x / scale) clamped to +-127.
-__device__ __forceinline__ int quant_value(float x, float scale) {
-    float q = roundf(__fdiv_rn(x, scale));
-    q = fminf(fmaxf(q, -127.0f), 127.0f);
-    return static_cast<int>(q);
-}
-
 // Quantise a shared-memory row of k floats (k % 16 == 0) to int8 `dst`.
 __device__ __forceinline__ void quantize_smem_row(const float* row, int k, float scale, int8_t* dst) {
+    const float inv = row_inv(scale);
     for (int i = threadIdx.x * 16; i < k; i += blockDim.x * 16) {
         uint32_t packed[4];
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
             const float4 v = *reinterpret_cast<const float4*>(row + i + 4 * w);
-            packed[w] = (quant_value(v.x, scale) & 0xFF) | ((quant_value(v.y, scale) & 0xFF) << 8) |
-                        ((quant_value(v.z, scale) & 0xFF) << 16) | ((quant_value(v.w, scale) & 0xFF) << 24);
+            packed[w] = quant_pack4(v, scale, inv);
         }
         *reinterpret_cast<uint4*>(dst + i) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
     }
@@ -159,8 +153,7 @@ __global__ void __launch_bounds__(kRowThreads) prep_w8_kernel(const uint8_t* __r
         if (threadIdx.x == 0) atomicExch(err, kErrNonFinite);
         return;
     }
-    const float mx = block_max(amax, red);
-    const float scale = mx == 0.0f ? 1.0f : __fdiv_rn(mx, 127.0f);
+    const float scale = row_scale(block_max(amax, red));
     quantize_smem_row(srow, k, scale, w + static_cast<size_t>(row) * k);
     if (threadIdx.x == 0) scales[row] = scale;
 }
@@ -220,13 +213,14 @@ __global__ void __launch_bounds__(kRowThreads) quant_rows_kernel(const float* __
         if (threadIdx.x == 0) atomicExch(err, kErrNonFinite);
         return;
     }
-    const float mx = block_max(amax, red);
-    const float scale = mx == 0.0f ? 1.0f : __fdiv_rn(mx, 127.0f);
+    const float scale = row_scale(block_max(amax, red));
     int8_t* dst = a8 + static_cast<size_t>(row) * ld8;
     if ((ld8 % 16) == 0 && (reinterpret_cast<uintptr_t>(a8) & 15) == 0 && k16 <= ld8) {
         quantize_smem_row(srow, k16, scale, dst);
     } else {
-        for (int i = threadIdx.x; i < k; i += kRowThreads) dst[i] = static_cast<int8_t>(quant_value(srow[i], scale));
+        const float inv = row_inv(scale);
+        for (int i = threadIdx.x; i < k; i += kRowThreads)
+            dst[i] = static_cast<int8_t>(quant_value(srow[i], scale, inv));
     }
     if (threadIdx.x == 0) scales[row] = scale;
 }

@@ -307,3 +307,86 @@ def test_capi_w8a8_m16(ctx, rng):
     out = np.empty((16, n), dtype=np.float32)
     assert ctx.matmul_w8a8_m16(w, s, a, out, k, n) == 0
     assert np.array_equal(_bits(out), _bits(oracle.matmul_w8a8(w, s, a)[1]))
+
+
+# ---- K2 fused into K3's prologue --------------------------------------------------
+
+@pytest.mark.parametrize("m,k,n", [(2, 112, 64), (77, 304, 200), (128, 2048, 5632), (512, 2048, 2560),
+                                   (600, 5632, 128), (1000, 1024, 1024), (16, 12288, 256)])
+def test_fused_quantiser_matches_oracle_and_unfused(ctx, rng, monkeypatch, m, k, n):
+    from rocknpu_b200 import device
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    a[:, rng.choice(k, max(1, k // 100), replace=False)] *= 20.0  # outlier channels
+    a[m // 2] = 0.0  # an all-zero token: scale 1.0
+    w8 = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
+    ws = rng.uniform(1e-3, 1e-2, size=n).astype(np.float32)
+    st, ref = oracle.matmul_w8a8(w8, ws, a)
+    assert st == 0
+    da, dw, dws = torch.from_numpy(a).cuda(), torch.from_numpy(w8).cuda(), torch.from_numpy(ws).cuda()
+    outs = {}
+    for fused in ("1", "0"):
+        monkeypatch.setenv("ROCKNPU_B200_FUSED_QUANT", fused)
+        for rep in range(2):  # the second launch reuses the self-cleared counters
+            out = torch.full((m, n), float("nan"), device="cuda")
+            device.matmul_w8a8(ctx, da, dw, dws, out)
+            assert rk.lib().rocknpu_b200_context_check(ctx.handle) == 0
+            outs[(fused, rep)] = out.cpu().numpy()
+    for key, got in outs.items():
+        assert np.array_equal(_bits(got), _bits(ref)), f"fused={key[0]} launch {key[1]} differs from the oracle"
+
+
+def test_fused_quantiser_flags_non_finite(ctx, rng, monkeypatch):
+    from rocknpu_b200 import device
+    monkeypatch.setenv("ROCKNPU_B200_FUSED_QUANT", "1")
+    m, k, n = 40, 512, 128
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    a[17, 300] = np.nan
+    w8 = torch.ones((n, k), dtype=torch.int8, device="cuda")
+    ws = torch.ones(n, device="cuda")
+    out = torch.empty((m, n), device="cuda")
+    device.matmul_w8a8(ctx, torch.from_numpy(a).cuda(), w8, ws, out)
+    assert rk.lib().rocknpu_b200_context_check(ctx.handle) == rk.STATUS_INVALID_ARGUMENT
+    a[17, 300] = 1.0
+    device.matmul_w8a8(ctx, torch.from_numpy(a).cuda(), w8, ws, out)  # counters were left clean
+    assert rk.lib().rocknpu_b200_context_check(ctx.handle) == 0
+
+
+def _near_half_rows(rng, m, k):
+    """Rows whose quotients x / scale sit within a few ulps of half-integers
+    (and on them), where a reciprocal multiply would round differently from
+    the IEEE quotient: scale = 127-multiple absmax / 127 fixed by one entry."""
+    rows = []
+    for i in range(m):
+        s0 = np.float32(rng.uniform(0.01, 3.0))
+        row = np.empty(k, dtype=np.float32)
+        row[0] = np.float32(127.0) * s0
+        j = rng.integers(-127, 127, size=k - 1).astype(np.float32) + np.float32(0.5)
+        x = (j * s0).astype(np.float32)
+        steps = rng.integers(-3, 4, size=k - 1)
+        for d in range(1, 4):  # nudge by up to 3 ulps either way
+            x = np.where(steps >= d, np.nextafter(x, np.float32(np.inf)), x)
+            x = np.where(steps <= -d, np.nextafter(x, np.float32(-np.inf)), x)
+        row[1:] = x
+        rows.append(row)
+    return np.stack(rows)
+
+
+def test_quantisers_round_like_the_ieee_quotient_near_half_integers(ctx, rng, monkeypatch, dev):
+    m, k, n = 64, 2048, 128
+    a = _near_half_rows(rng, m, k)
+    st, q_ref, s_ref = oracle.quantize_rows(a)
+    assert st == 0
+    status = dev.new_status()
+    q, s = dev.quantize_rows(torch.from_numpy(a).cuda(), status)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    assert np.array_equal(q.cpu().numpy(), q_ref) and np.array_equal(_bits(s.cpu().numpy()), _bits(s_ref))
+    # the fused prologue quantiser: checked through the W8A8 output
+    w8 = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
+    ws = rng.uniform(1e-3, 1e-2, size=n).astype(np.float32)
+    st, ref = oracle.matmul_w8a8(w8, ws, a)
+    monkeypatch.setenv("ROCKNPU_B200_FUSED_QUANT", "1")
+    out = torch.empty((m, n), device="cuda")
+    dev.matmul_w8a8(ctx, torch.from_numpy(a).cuda(), torch.from_numpy(w8).cuda(), torch.from_numpy(ws).cuda(), out)
+    assert rk.lib().rocknpu_b200_context_check(ctx.handle) == 0
+    assert np.array_equal(_bits(out.cpu().numpy()), _bits(ref))
