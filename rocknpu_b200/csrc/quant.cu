@@ -26,19 +26,30 @@ __device__ __forceinline__ float half_bits_to_float(uint32_t bits) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(bits & 0xFFFFu)));
 }
 
-// 6-bit scale/min pair j of a Q4_K/Q5_K superblock; s[] holds its 12 bytes.
-__device__ __forceinline__ void scale_min_k4(int j, const uint8_t* s, int& sc, int& m) {
+// Byte i (0..11) of the 12 scale bytes held in three little-endian words.
+__device__ __forceinline__ int scale_byte(const uint32_t (&s)[3], int i) {
+    const uint32_t w = i < 4 ? s[0] : (i < 8 ? s[1] : s[2]);
+    return static_cast<int>((w >> (8 * (i & 3))) & 0xFFu);
+}
+
+// 6-bit scale/min pair j of a Q4_K/Q5_K superblock (ggml's K-quant scale
+// packing: j < 4 in the low 6 bits of bytes j / j+4, j >= 4 split between
+// the nibbles of byte j+4 and the top bits of bytes j-4 / j).
+__device__ __forceinline__ void scale_min_k4(int j, const uint32_t (&s)[3], int& sc, int& m) {
     if (j < 4) {
-        sc = s[j] & 63;
-        m = s[j + 4] & 63;
+        sc = scale_byte(s, j) & 63;
+        m = scale_byte(s, j + 4) & 63;
     } else {
-        sc = (s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4);
-        m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+        sc = (scale_byte(s, j + 4) & 0x0F) | ((scale_byte(s, j - 4) >> 6) << 4);
+        m = (scale_byte(s, j + 4) >> 4) | ((scale_byte(s, j) >> 6) << 4);
     }
 }
 
 // Dequantise the 8 values that thread `l` (0..31) owns in one superblock and
-// hand them to `put(index_in_block, value)`.  Value formulas follow the
+// hand them to `put(slot, index_in_block, value)`; slot 0..7 is a fixed
+// per-lane order (Q4_K/Q5_K: slots 0-3 are 4 consecutive values at
+// 64g + 4(l%8), slots 4-7 the 4 at 32 further; Q6_K: slots t and 4 + t are the
+// 2 consecutive values at 128h + 2(l%16) + 32t).  Value formulas follow the
 // llama-gguf dequantisers the reference calls (capi/src/lib.rs:732-733,
 // 986-988): Q4_K/Q5_K (d*sc)*q - (dmin*m), Q6_K (d*sc)*(q-32), f32 each step.
 template <int KIND, class Put>
@@ -46,10 +57,7 @@ __device__ __forceinline__ void dequant8(const uint8_t* blk, int l, Put&& put) {
     if constexpr (KIND == kQ4K || KIND == kQ5K) {
         const uint32_t dd = ld32(blk);
         const float d = half_bits_to_float(dd), dmin = half_bits_to_float(dd >> 16);
-        uint8_t s[12];
-        *reinterpret_cast<uint32_t*>(s) = ld32(blk + 4);
-        *reinterpret_cast<uint32_t*>(s + 4) = ld32(blk + 8);
-        *reinterpret_cast<uint32_t*>(s + 8) = ld32(blk + 12);
+        const uint32_t s[3] = {ld32(blk + 4), ld32(blk + 8), ld32(blk + 12)};
         const int g = l >> 3, i4 = (l & 7) * 4;
         int sc, mn;
         scale_min_k4(2 * g, s, sc, mn);
@@ -67,8 +75,8 @@ __device__ __forceinline__ void dequant8(const uint8_t* blk, int l, Put&& put) {
                 lo |= ((hb >> (2 * g)) & 1) << 4;
                 hi |= ((hb >> (2 * g + 1)) & 1) << 4;
             }
-            put(64 * g + i4 + i, __fsub_rn(__fmul_rn(d1, static_cast<float>(lo)), m1));
-            put(64 * g + 32 + i4 + i, __fsub_rn(__fmul_rn(d2, static_cast<float>(hi)), m2));
+            put(i, 64 * g + i4 + i, __fsub_rn(__fmul_rn(d1, small_uint_to_float(lo)), m1));
+            put(4 + i, 64 * g + 32 + i4 + i, __fsub_rn(__fmul_rn(d2, small_uint_to_float(hi)), m2));
         }
     } else {
         const float d = half_bits_to_float(ld16(blk + 208));
@@ -83,15 +91,16 @@ __device__ __forceinline__ void dequant8(const uint8_t* blk, int l, Put&& put) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
             const uint32_t a = (qa >> (8 * e)) & 0xFF, b = (qb >> (8 * e)) & 0xFF, hb = (qh >> (8 * e)) & 0xFF;
-            const int q0 = static_cast<int>((a & 0x0F) | ((hb & 3) << 4)) - 32;
-            const int q1 = static_cast<int>((b & 0x0F) | (((hb >> 2) & 3) << 4)) - 32;
-            const int q2 = static_cast<int>((a >> 4) | (((hb >> 4) & 3) << 4)) - 32;
-            const int q3 = static_cast<int>((b >> 4) | (((hb >> 6) & 3) << 4)) - 32;
+            // q - 32 as an exact float: (2^23 + q) - (2^23 + 32)
+            const uint32_t q0 = (a & 0x0F) | ((hb & 3) << 4);
+            const uint32_t q1 = (b & 0x0F) | (((hb >> 2) & 3) << 4);
+            const uint32_t q2 = (a >> 4) | (((hb >> 4) & 3) << 4);
+            const uint32_t q3 = (b >> 4) | (((hb >> 6) & 3) << 4);
             const int base = 128 * h + lp + e;
-            put(base, __fmul_rn(ds[0], static_cast<float>(q0)));
-            put(base + 32, __fmul_rn(ds[1], static_cast<float>(q1)));
-            put(base + 64, __fmul_rn(ds[2], static_cast<float>(q2)));
-            put(base + 96, __fmul_rn(ds[3], static_cast<float>(q3)));
+            put(4 * e + 0, base, __fmul_rn(ds[0], __fsub_rn(__uint_as_float(0x4B000000u | q0), 8388640.0f)));
+            put(4 * e + 1, base + 32, __fmul_rn(ds[1], __fsub_rn(__uint_as_float(0x4B000000u | q1), 8388640.0f)));
+            put(4 * e + 2, base + 64, __fmul_rn(ds[2], __fsub_rn(__uint_as_float(0x4B000000u | q2), 8388640.0f)));
+            put(4 * e + 3, base + 96, __fmul_rn(ds[3], __fsub_rn(__uint_as_float(0x4B000000u | q3), 8388640.0f)));
         }
     }
 }
@@ -143,7 +152,7 @@ __global__ void __launch_bounds__(kRowThreads) prep_w8_kernel(const uint8_t* __r
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int b = warp; b < nb; b += kRowThreads / 32) {
         float* dst = srow + b * 256;
-        dequant8<KIND>(src + b * bb, lane, [&](int idx, float v) {
+        dequant8<KIND>(src + b * bb, lane, [&](int, int idx, float v) {
             dst[idx] = v;
             finite &= isfinite(v);
             amax = fmaxf(amax, fabsf(v));
@@ -155,6 +164,70 @@ __global__ void __launch_bounds__(kRowThreads) prep_w8_kernel(const uint8_t* __r
     }
     const float scale = row_scale(block_max(amax, red));
     quantize_smem_row(srow, k, scale, w + static_cast<size_t>(row) * k);
+    if (threadIdx.x == 0) scales[row] = scale;
+}
+
+// K1 for rows of up to 8 * BPW superblocks (k <= 16384): the same
+// arithmetic as prep_w8_kernel with the dequantised row held in registers
+// (8 values per lane per superblock) instead of shared memory, so many more
+// rows are in flight per SM and every superblock's loads are issued before
+// any value is used.  Stores follow dequant8's slot layout: 4-byte words
+// (Q4_K/Q5_K) or 2-byte pairs (Q6_K), coalesced across the warp.
+template <int KIND, int BPW>
+__global__ void __launch_bounds__(kRowThreads) prep_w8_reg_kernel(const uint8_t* __restrict__ blocks, int k,
+                                                                   int8_t* __restrict__ w, float* __restrict__ scales,
+                                                                   int* __restrict__ err) {
+    __shared__ float red[33];
+    const int row = blockIdx.x;
+    const int nb = k >> 8;
+    const size_t bb = KIND == kQ4K ? 144 : KIND == kQ5K ? 176 : 210;
+    const uint8_t* src = blocks + static_cast<size_t>(row) * nb * bb;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float v[BPW][8];
+    float amax = 0.0f;
+    bool finite = true;
+#pragma unroll
+    for (int i = 0; i < BPW; ++i) {
+        const int b = warp + 8 * i;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;
+        if (b < nb) {
+            dequant8<KIND>(src + b * bb, lane, [&](int slot, int, float x) {
+                v[i][slot] = x;
+                finite &= isfinite(x);
+                amax = fmaxf(amax, fabsf(x));
+            });
+        }
+    }
+    if (__syncthreads_or(!finite)) {
+        if (threadIdx.x == 0) atomicExch(err, kErrNonFinite);
+        return;
+    }
+    const float scale = row_scale(block_max(amax, red));
+    const float inv = row_inv(scale);
+    int8_t* dst = w + static_cast<size_t>(row) * k;
+#pragma unroll
+    for (int i = 0; i < BPW; ++i) {
+        const int b = warp + 8 * i;
+        if (b < nb) {
+            int8_t* out = dst + b * 256;
+            if constexpr (KIND == kQ4K || KIND == kQ5K) {
+                const int off = 64 * (lane >> 3) + (lane & 7) * 4;
+                *reinterpret_cast<uint32_t*>(out + off) =
+                    quant_pack4(make_float4(v[i][0], v[i][1], v[i][2], v[i][3]), scale, inv);
+                *reinterpret_cast<uint32_t*>(out + off + 32) =
+                    quant_pack4(make_float4(v[i][4], v[i][5], v[i][6], v[i][7]), scale, inv);
+            } else {
+                const int off = 128 * (lane >> 4) + (lane & 15) * 2;
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const uint32_t lo = quant_value(v[i][t], scale, inv) & 0xFF;
+                    const uint32_t hi = quant_value(v[i][4 + t], scale, inv) & 0xFF;
+                    *reinterpret_cast<uint16_t*>(out + off + 32 * t) = static_cast<uint16_t>(lo | (hi << 8));
+                }
+            }
+        }
+    }
     if (threadIdx.x == 0) scales[row] = scale;
 }
 
@@ -171,7 +244,7 @@ __global__ void __launch_bounds__(kRowThreads) dequant_f16_kernel(const uint8_t*
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int b = warp; b < nb; b += kRowThreads / 32) {
         __half* dst = out + b * 256;
-        dequant8<KIND>(src + b * bb, lane, [&](int idx, float v) { dst[idx] = __float2half_rn(v); });
+        dequant8<KIND>(src + b * bb, lane, [&](int, int idx, float v) { dst[idx] = __float2half_rn(v); });
     }
 }
 
@@ -252,10 +325,29 @@ void set_smem(F* f, size_t bytes) {
     if (bytes > 40 * 1024) cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
 }
 
+template <int KIND, int BPW>
+bool launch_prep_reg(int bpw, const uint8_t* blocks, int k, int n, int8_t* w, float* scales, int* err,
+                     cudaStream_t s) {
+    if constexpr (BPW > 8) {
+        return false;
+    } else {
+        if (bpw != BPW) return launch_prep_reg<KIND, BPW + 1>(bpw, blocks, k, n, w, scales, err, s);
+        prep_w8_reg_kernel<KIND, BPW><<<n, kRowThreads, 0, s>>>(blocks, k, w, scales, err);
+        return true;
+    }
+}
+
 }  // namespace
 
 void launch_prep_w8(int kind, const uint8_t* blocks, int k, int n, int8_t* w, float* scales, int* err,
                     cudaStream_t s) {
+    // rows of up to 64 superblocks: the register kernel
+    const int bpw = ((k >> 8) + 7) / 8;
+    if (bpw <= 8) {
+        if (kind == kQ4K && launch_prep_reg<kQ4K, 1>(bpw, blocks, k, n, w, scales, err, s)) return;
+        if (kind == kQ5K && launch_prep_reg<kQ5K, 1>(bpw, blocks, k, n, w, scales, err, s)) return;
+        if (kind == kQ6K && launch_prep_reg<kQ6K, 1>(bpw, blocks, k, n, w, scales, err, s)) return;
+    }
     const size_t smem = static_cast<size_t>(k) * sizeof(float);
     if (kind == kQ4K) {
         set_smem(prep_w8_kernel<kQ4K>, smem);

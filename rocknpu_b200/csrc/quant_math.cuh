@@ -47,30 +47,43 @@ static __device__ __noinline__ uint32_t quant_pack4_slow(float4 v, float scale) 
            ((quant_value_exact(v.z, scale) & 0xFF) << 16) | ((quant_value_exact(v.w, scale) & 0xFF) << 24);
 }
 
-// rint(x * inv) clamped, and whether the rounding test failed: |t - r| is
-// exact (Sterbenz); NaN / inf fail the test too.
-__device__ __forceinline__ int quant_candidate(float x, float inv, bool& doubtful) {
+// Adding 1.5 * 2^23 to |t| < 2^22 rounds it to an integer (ties to even) in
+// one FADD; the sum's low mantissa bits then hold that integer in two's
+// complement, so its low byte is the int8 value without a conversion.
+constexpr float kRoundMagic = 12582912.0f;
+
+// Candidate int8 (in the low byte of the result) for t = x * inv, and whether
+// the rounding test failed: |t - rint(t)| is exact (Sterbenz); NaN / inf, and
+// |t| above 127.25 (outside the bound the test assumes; the exact path
+// clamps), fail it too.
+__device__ __forceinline__ uint32_t quant_candidate(float x, float inv, bool& doubtful) {
     const float t = __fmul_rn(x, inv);
-    const float r = rintf(t);
-    doubtful |= !(fabsf(__fsub_rn(t, r)) <= 0.49996f);
-    return static_cast<int>(fminf(fmaxf(r, -127.0f), 127.0f));
+    const float m = __fadd_rn(t, kRoundMagic);
+    const float r = __fsub_rn(m, kRoundMagic);
+    doubtful |= !(fabsf(__fsub_rn(t, r)) <= 0.49996f) || !(fabsf(t) <= 127.25f);
+    return __float_as_uint(m);
 }
 
 // The same integer as quant_value_exact for every x of a row whose absmax
 // gave `scale` (see the rounding test above); inv = row_inv(scale).
 __device__ __forceinline__ int quant_value(float x, float scale, float inv) {
     bool doubtful = false;
-    const int q = quant_candidate(x, inv, doubtful);
-    return doubtful ? quant_value_slow(x, scale) : q;
+    const uint32_t q = quant_candidate(x, inv, doubtful);
+    return doubtful ? quant_value_slow(x, scale) : static_cast<int>(static_cast<int8_t>(q & 0xFFu));
 }
 
 __device__ __forceinline__ uint32_t quant_pack4(float4 v, float scale, float inv) {
     bool doubtful = false;
-    const uint32_t w = (quant_candidate(v.x, inv, doubtful) & 0xFF) |
-                       ((quant_candidate(v.y, inv, doubtful) & 0xFF) << 8) |
-                       ((quant_candidate(v.z, inv, doubtful) & 0xFF) << 16) |
-                       ((quant_candidate(v.w, inv, doubtful) & 0xFF) << 24);
+    const uint32_t a = quant_candidate(v.x, inv, doubtful), b = quant_candidate(v.y, inv, doubtful);
+    const uint32_t c = quant_candidate(v.z, inv, doubtful), d = quant_candidate(v.w, inv, doubtful);
+    const uint32_t w = __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
     return doubtful ? quant_pack4_slow(v, scale) : w;
+}
+
+// Exact float of a small non-negative integer (< 2^23) without the
+// quarter-rate integer-to-float conversion: 2^23 + i has i in its mantissa.
+__device__ __forceinline__ float small_uint_to_float(uint32_t i) {
+    return __fsub_rn(__uint_as_float(0x4B000000u | i), 8388608.0f);
 }
 
 __device__ __forceinline__ float warp_max(float v) {
