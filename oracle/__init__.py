@@ -67,6 +67,10 @@ def lib():
         L.orc_matmul_f16.argtypes = [P, P, P, S, S, S]
         L.orc_swiglu.restype = None
         L.orc_swiglu.argtypes = [P, P, P, S]
+        L.orc_hilo_stack.restype = ctypes.c_int
+        L.orc_hilo_stack.argtypes = [P, S, S, P]
+        L.orc_hilo_sum.restype = None
+        L.orc_hilo_sum.argtypes = [P, S, P]
         L.orc_split_blocks.restype = S
         L.orc_split_blocks.argtypes = [S, S, S, P, P]
         L.orc_threads.restype = ctypes.c_int
@@ -172,6 +176,35 @@ def swiglu(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
     out = np.empty_like(gate)
     lib().orc_swiglu(_p(gate), _p(up), _p(out), gate.size)
     return out
+
+
+def hilo_stack(a: np.ndarray):
+    """(status, stacked [2m, k]) of the two-part activation encoding."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    m, k = a.shape
+    out = np.empty((2 * m, k), dtype=np.float32)
+    st = lib().orc_hilo_stack(_p(a), m, k, _p(out))
+    return st, out
+
+
+def hilo_sum(stacked: np.ndarray) -> np.ndarray:
+    stacked = np.ascontiguousarray(stacked, dtype=np.float32)
+    half = stacked.shape[0] // 2
+    out = np.empty((half,) + stacked.shape[1:], dtype=np.float32)
+    lib().orc_hilo_sum(_p(stacked), out.size, _p(out))
+    return out
+
+
+def matmul_w8a8_hilo(w: np.ndarray, w_scales: np.ndarray, a: np.ndarray):
+    """The reference's HILO prompt projection: W8A8 over [x; residual(x)],
+    then the two output halves summed (capi/src/lib.rs:4981-5001)."""
+    st, stacked = hilo_stack(a)
+    if st != 0:
+        return st, None
+    st, y = matmul_w8a8(w, w_scales, stacked)
+    if st != 0:
+        return st, None
+    return 0, hilo_sum(y)
 
 
 def split_blocks(blocks: int, block_width: int, workers: int):

@@ -352,6 +352,43 @@ void orc_swiglu(const float *gate, const float *up, float *out, size_t n) {
     }
 }
 
+/* hilo_stack (capi/src/lib.rs:2045-2070): rows [x; residual(x)] of the
+ * two-part activation encoding, residual = x - f32(q) * scale with q, scale
+ * from quantize_symmetric_into (two f32 roundings, no fused multiply-add).
+ * `stacked` is [2m][k]; returns ORC_INVALID_ARGUMENT when a row does not
+ * quantise (non-finite), where the reference takes its normal path. */
+int orc_hilo_stack(const float *a, size_t m, size_t k, float *stacked) {
+    int status = ORC_OK;
+    memcpy(stacked, a, m * k * sizeof(float));
+#pragma omp parallel
+    {
+        int8_t *q = (int8_t *)malloc(k);
+#pragma omp for schedule(static)
+        for (long r = 0; r < (long)m; ++r) {
+            const float *x = a + (size_t)r * k;
+            float *res = stacked + (m + (size_t)r) * k;
+            float scale;
+            if (orc_quantize_symmetric_into(x, k, q, &scale) != ORC_OK) {
+#pragma omp atomic write
+                status = ORC_INVALID_ARGUMENT;
+                continue;
+            }
+            for (size_t i = 0; i < k; ++i) {
+                const float back = (float)q[i] * scale;
+                res[i] = x[i] - back;
+            }
+        }
+        free(q);
+    }
+    return status;
+}
+
+/* hilo_sum (capi/src/lib.rs:2073-2083): out[i] = hi[i] + lo[i] over the two
+ * halves of the stacked output [2][len]. */
+void orc_hilo_sum(const float *stacked, size_t len, float *out) {
+    for (size_t i = 0; i < len; ++i) out[i] = stacked[i] + stacked[len + i];
+}
+
 /* split_blocks (rocknpu-matmul/src/int8_decode_pool.rs:1505-1522): an even
  * split of `blocks` blocks over `workers`, remainder to the first workers. */
 size_t orc_split_blocks(size_t blocks, size_t block_width, size_t workers, size_t *starts,

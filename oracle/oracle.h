@@ -66,6 +66,9 @@ void orc_matmul_f16(const uint16_t *w_bits, const float *a, float *out, size_t m
 
 void orc_swiglu(const float *gate, const float *up, float *out, size_t n);
 
+int orc_hilo_stack(const float *a, size_t m, size_t k, float *stacked);
+void orc_hilo_sum(const float *stacked, size_t len, float *out);
+
 size_t orc_split_blocks(size_t blocks, size_t block_width, size_t workers, size_t *starts,
                         size_t *widths);
 

@@ -245,6 +245,8 @@ struct RockNpuContext {
     DevBuf a_f32, a_i8, a_scale, a_f16, out_f32, staging, swiglu_tmp;
     DevBuf gemm_ws;      // split-K workspace, all-zero between launches
     DevBuf quant_sync;   // fused-quantiser counters, all-zero between launches
+    DevBuf hilo_a, hilo_out;  // HILO stacked activations [2m][k], summed outputs
+    bool in_hilo = false;     // inside a HILO-encoded call (HiloInner, L:2025-2043)
 
     // Prompt-path (M-tile) resident weights: single projections and
     // concatenated same-input groups (L:1808-1849, L:2351-2384).
@@ -409,16 +411,46 @@ size_t chunk_rows(size_t m, size_t k, size_t total_n) {
 // resident int8 weight, member outputs copied back, pipelined over row
 // chunks on three streams.  On INVALID_ARGUMENT (a non-finite activation)
 // output rows of chunks that were already copied back hold their results.
+// With `dev_a` the activations are already in device memory (one chunk, no
+// copy in), and with `keep` the outputs stay in c->out_f32 (member i's
+// [m][n_i] block at column offset start_i * m) instead of being copied out.
 int run_w8a8(Ctx* c, const PreparedW8& pw, const float* host_a, size_t m, size_t k, const OutSeg* segs, size_t nseg,
-             bool m1_overlap) {
+             bool m1_overlap, const float* dev_a = nullptr, bool keep = false) {
     const size_t ld8 = round_up(k, 16);
     const size_t total_n = pw.n;
-    if (c->a_f32.ensure(m * k * sizeof(float)) || c->a_i8.ensure(m * ld8) || c->a_scale.ensure(m * sizeof(float)) ||
-        c->out_f32.ensure(m * total_n * sizeof(float)))
+    if ((!dev_a && c->a_f32.ensure(m * k * sizeof(float))) || c->a_i8.ensure(m * ld8) ||
+        c->a_scale.ensure(m * sizeof(float)) || c->out_f32.ensure(m * total_n * sizeof(float)))
         return kExecError;
     int st = reset_status(c);
     if (st != kOk) return st;
     float* out = c->out_f32.as<float>();
+    if (dev_a) {
+        rk::GemmWorkspace gws;
+        if (context_ws(c, m, total_n, k, &gws) != kOk) return kExecError;
+        rk::OutMembers om;
+        om.count = static_cast<int>(nseg);
+        size_t start = 0;
+        for (size_t i = 0; i < nseg; ++i) {
+            om.n_start[i] = static_cast<int>(start);
+            om.out[i] = out + m * start;
+            om.ldo[i] = static_cast<long long>(segs[i].n);
+            start += segs[i].n;
+        }
+        om.n_start[nseg] = static_cast<int>(start);
+        if (launch_w8a8(c, pw.w, pw.scales, dev_a, m, k, total_n, c->a_i8.as<int8_t>(), ld8, c->a_scale.as<float>(),
+                        om, &gws, c->stream) != cudaSuccess)
+            return kExecError;
+        st = finish(c);
+        if (st != kOk || keep) return st;
+        start = 0;
+        for (size_t i = 0; i < nseg; ++i) {
+            if (cudaMemcpyAsync(segs[i].host, out + m * start, m * segs[i].n * sizeof(float), cudaMemcpyDeviceToHost,
+                                c->stream))
+                return kExecError;
+            start += segs[i].n;
+        }
+        return cuda_status(cudaStreamSynchronize(c->stream));
+    }
     float* a_dev = c->a_f32.as<float>();
     int8_t* a8 = c->a_i8.as<int8_t>();
     float* as = c->a_scale.as<float>();
@@ -496,19 +528,22 @@ int run_w8a8(Ctx* c, const PreparedW8& pw, const float* host_a, size_t m, size_t
     return st != kOk ? st : st2;
 }
 
-// FP16 executor on resident f16 rows: f16(a) . w^T in f32.
-int run_f16(Ctx* c, const PreparedF16& pw, const float* host_a, size_t m, size_t k, float* host_out) {
+// FP16 executor on resident f16 rows: f16(a) . w^T in f32.  `dev_a` and
+// `keep` as for run_w8a8 (the output stays in c->out_f32 as [m][n]).
+int run_f16(Ctx* c, const PreparedF16& pw, const float* host_a, size_t m, size_t k, float* host_out,
+            const float* dev_a = nullptr, bool keep = false) {
     const size_t ldh = round_up(k, 8);
     const size_t n = pw.n;
-    if (c->a_f32.ensure(m * k * sizeof(float)) || c->a_f16.ensure(m * ldh * sizeof(__half)) ||
+    if ((!dev_a && c->a_f32.ensure(m * k * sizeof(float))) || c->a_f16.ensure(m * ldh * sizeof(__half)) ||
         c->out_f32.ensure(m * n * sizeof(float)))
         return kExecError;
     int st = reset_status(c);
     if (st != kOk) return st;
-    if (cudaMemcpyAsync(c->a_f32.ptr, host_a, m * k * sizeof(float), cudaMemcpyHostToDevice, c->stream))
+    if (!dev_a &&
+        cudaMemcpyAsync(c->a_f32.ptr, host_a, m * k * sizeof(float), cudaMemcpyHostToDevice, c->stream))
         return kExecError;
-    rk::launch_f32_to_f16(c->a_f32.as<float>(), static_cast<int>(m), static_cast<int>(k), static_cast<long long>(k),
-                          c->a_f16.as<__half>(), static_cast<long long>(ldh), c->stream);
+    rk::launch_f32_to_f16(dev_a ? dev_a : c->a_f32.as<float>(), static_cast<int>(m), static_cast<int>(k),
+                          static_cast<long long>(k), c->a_f16.as<__half>(), static_cast<long long>(ldh), c->stream);
     rk::OutMembers om;
     om.count = 1;
     om.n_start[1] = static_cast<int>(n);
@@ -519,7 +554,7 @@ int run_f16(Ctx* c, const PreparedF16& pw, const float* host_a, size_t m, size_t
                                      static_cast<int>(k), nullptr, nullptr, om, nullptr, 0, c->d_status, c->stream);
     if (e != cudaSuccess) return kExecError;
     st = finish(c);
-    if (st != kOk) return st;
+    if (st != kOk || keep) return st;
     if (cudaMemcpyAsync(host_out, c->out_f32.ptr, m * n * sizeof(float), cudaMemcpyDeviceToHost, c->stream))
         return kExecError;
     return cuda_status(cudaStreamSynchronize(c->stream));
@@ -566,7 +601,7 @@ bool bind(Ctx* c) { return cudaSetDevice(c->device) == cudaSuccess; }
 // Prompt-path single projection with K-quant weights (every W8A8 branch of
 // L:4933-5256).
 int q_prompt_w8a8(Ctx* c, int kind, const uint8_t* w, size_t bytes, const float* a, float* out, size_t m, size_t k,
-                  size_t n) {
+                  size_t n, const float* dev_a = nullptr, bool keep = false) {
     const uint64_t t0 = c->profile ? now_ns() : 0;
     const Key key = make_key(w, bytes, k, n, kind);
     auto it = c->mtile.find(key);
@@ -583,7 +618,7 @@ int q_prompt_w8a8(Ctx* c, int kind, const uint8_t* w, size_t bytes, const float*
         c->mtile_hits++;
     }
     OutSeg seg{out, n};
-    const int st = run_w8a8(c, *it->second, a, m, k, &seg, 1, false);
+    const int st = run_w8a8(c, *it->second, a, m, k, &seg, 1, false, dev_a, keep);
     if (c->profile) {
         c->mtile_calls++;
         c->mtile_ns += now_ns() - t0;
@@ -592,7 +627,7 @@ int q_prompt_w8a8(Ctx* c, int kind, const uint8_t* w, size_t bytes, const float*
 }
 
 int q_prompt_f16(Ctx* c, int kind, const uint8_t* w, size_t bytes, const float* a, float* out, size_t m, size_t k,
-                 size_t n) {
+                 size_t n, const float* dev_a = nullptr, bool keep = false) {
     const Key key = make_key(w, bytes, k, n, kind);
     F16Ptr p;
     auto it = c->f16.find(key);
@@ -605,7 +640,7 @@ int q_prompt_f16(Ctx* c, int kind, const uint8_t* w, size_t bytes, const float* 
         // ROCKNPU_PREFILL_CACHE; the uncached bridge re-decodes per call.
         if (env_enabled("ROCKNPU_PREFILL_CACHE")) c->f16.emplace(key, p);
     }
-    return run_f16(c, *p, a, m, k, out);
+    return run_f16(c, *p, a, m, k, out, dev_a, keep);
 }
 
 // M=1 through the decode cache (execute_cached_w8a8_m1, L:1567-1701 and the
@@ -661,6 +696,63 @@ bool scales_valid(const float* s, size_t n) {
 
 bool mul_overflows(size_t a, size_t b, size_t* out) { return __builtin_mul_overflow(a, b, out); }
 
+// ROCKNPU_PREFILL_HILO (hilo_mode, L:2005-2023): 0 off, 1 "down" (wide-K
+// projections only), 2 "1"/"all".
+int hilo_mode() {
+    const char* v = std::getenv("ROCKNPU_PREFILL_HILO");
+    if (!v) return 0;
+    if (std::strcmp(v, "1") == 0 || std::strcmp(v, "all") == 0) return 2;
+    if (std::strcmp(v, "down") == 0) return 1;
+    return 0;
+}
+
+// hilo_stack's conditions (L:2045-2053), outside an encoded call.
+bool hilo_applies(const Ctx* c, size_t m, size_t k) {
+    const int mode = hilo_mode();
+    if (mode == 0 || m < 2 || k == 0 || c->in_hilo) return false;
+    return !(mode == 1 && k <= 4096 && k % 512 == 0);
+}
+
+// Two-part activation encoding around one prompt call (L:2484-2513,
+// 4981-5001, 5428-5448): rows [x; x - dequant(quant(x))] go through `inner`
+// as 2m device-resident rows, and the two halves of each member's output are
+// summed (hilo_sum) into the caller's buffers.  A row that does not quantise
+// (non-finite) sends the reference down its normal path; `normal` is that.
+template <class Inner, class Normal>
+int hilo_call(Ctx* c, const float* host_a, size_t m, size_t k, const OutSeg* segs, size_t nseg, Inner&& inner,
+              Normal&& normal) {
+    if (c->hilo_a.ensure(2 * m * k * sizeof(float)) != cudaSuccess) return kExecError;
+    float* stacked = c->hilo_a.as<float>();
+    int st = reset_status(c);
+    if (st != kOk) return st;
+    if (cudaMemcpyAsync(stacked, host_a, m * k * sizeof(float), cudaMemcpyHostToDevice, c->stream)) return kExecError;
+    rk::launch_hilo_residual(stacked, static_cast<int>(m), static_cast<int>(k), static_cast<long long>(k),
+                             stacked + m * k, static_cast<long long>(k), c->d_status, c->stream);
+    if (cudaGetLastError() != cudaSuccess) return kExecError;
+    st = finish(c);
+    if (st == kInvalid) return normal();
+    if (st != kOk) return st;
+    c->in_hilo = true;
+    st = inner(stacked, 2 * m);
+    c->in_hilo = false;
+    if (st != kOk) return st;
+    size_t total = 0;
+    for (size_t i = 0; i < nseg; ++i) total += segs[i].n;
+    if (c->hilo_out.ensure(m * total * sizeof(float)) != cudaSuccess) return kExecError;
+    const float* y = c->out_f32.as<float>();
+    float* sum = c->hilo_out.as<float>();
+    size_t start = 0;
+    for (size_t i = 0; i < nseg; ++i) {
+        const size_t len = m * segs[i].n;
+        const float* blk = y + 2 * m * start;  // member i's [2m][n_i] block
+        rk::launch_add_halves(blk, blk + len, sum + m * start, static_cast<long long>(len), c->stream);
+        if (cudaMemcpyAsync(segs[i].host, sum + m * start, len * sizeof(float), cudaMemcpyDeviceToHost, c->stream))
+            return kExecError;
+        start += segs[i].n;
+    }
+    return cuda_status(cudaStreamSynchronize(c->stream));
+}
+
 // Shared body of rocknpu_matmul_q{4,5,6}_k_f32_f32.
 int matmul_q(Ctx* c, int kind, const uint8_t* w, size_t bytes, const float* a, float* out, size_t m, size_t k,
              size_t n) {
@@ -682,11 +774,20 @@ int matmul_q(Ctx* c, int kind, const uint8_t* w, size_t bytes, const float* a, f
         OutSeg seg{out, n};
         return decode_m1(c, KeyList{key}, &mb, 1, a, &seg, k);
     }
-    switch (route_q46_prompt(m, k, n)) {
-        case Route::W8A8: return q_prompt_w8a8(c, kind, w, bytes, a, out, m, k, n);
-        case Route::FP16: return q_prompt_f16(c, kind, w, bytes, a, out, m, k, n);
-        default: return kInvalid;
+    auto route = [&](const float* host, const float* dev, size_t rows, bool keep) {
+        switch (route_q46_prompt(rows, k, n)) {
+            case Route::W8A8: return q_prompt_w8a8(c, kind, w, bytes, host, out, rows, k, n, dev, keep);
+            case Route::FP16: return q_prompt_f16(c, kind, w, bytes, host, out, rows, k, n, dev, keep);
+            default: return kInvalid;
+        }
+    };
+    if (native_routes() && hilo_applies(c, m, k)) {
+        OutSeg seg{out, n};
+        return hilo_call(
+            c, a, m, k, &seg, 1, [&](const float* dev, size_t rows) { return route(nullptr, dev, rows, true); },
+            [&] { return route(a, nullptr, m, false); });
     }
+    return route(a, nullptr, m, false);
 }
 
 int quant_kind46(uint32_t kind) { return kind == 4 ? rk::kQ4K : kind == 6 ? rk::kQ6K : 0; }
@@ -694,7 +795,8 @@ int quant_kind46(uint32_t kind) { return kind == 4 ? rk::kQ4K : kind == 6 ? rk::
 // Concatenated-N prompt group (execute_cached_w8a8_mtile_concat, L:2262-2424):
 // one GEMM over the group's resident rows, member outputs split by column.
 int concat_group(Ctx* c, size_t count, const uint8_t* const* weights, const size_t* bytes, const int* kinds,
-                 const size_t* ns, const float* a, float* const* outs, size_t m, size_t k) {
+                 const size_t* ns, const float* a, float* const* outs, size_t m, size_t k, const float* dev_a = nullptr,
+                 bool keep = false) {
     KeyList keys;
     std::vector<Member> members;
     std::vector<OutSeg> segs;
@@ -715,8 +817,9 @@ int concat_group(Ctx* c, size_t count, const uint8_t* const* weights, const size
     } else {
         c->mtile_hits++;
     }
-    return run_w8a8(c, *it->second, a, m, k, segs.data(), count, false);
+    return run_w8a8(c, *it->second, a, m, k, segs.data(), count, false, dev_a, keep);
 }
+
 
 }  // namespace
 
@@ -806,7 +909,7 @@ void rocknpu_context_destroy(rocknpu_context* context) {
     c->decode_groups.clear();
     c->f16.clear();
     for (DevBuf* b : {&c->a_f32, &c->a_i8, &c->a_scale, &c->a_f16, &c->out_f32, &c->staging, &c->swiglu_tmp,
-                      &c->gemm_ws, &c->quant_sync})
+                      &c->gemm_ws, &c->quant_sync, &c->hilo_a, &c->hilo_out})
         b->release();
     if (c->d_status) cudaFree(c->d_status);
     if (c->h_status) cudaFreeHost(c->h_status);
@@ -864,6 +967,16 @@ int rocknpu_matmul_q_concat_f32_f32_mtile(rocknpu_context* context, size_t count
     for (size_t i = 0; i < count; ++i)
         if (bytes[i] != ns[i] * (k / 256) * rk::qblock_bytes(kd[i])) return kInvalid;
     if (!bind(context)) return kDeviceError;
+    if (hilo_applies(context, m, k)) {
+        OutSeg segs[4];
+        for (size_t i = 0; i < count; ++i) segs[i] = OutSeg{outputs[i], ns[i]};
+        return hilo_call(
+            context, a, m, k, segs, count,
+            [&](const float* dev, size_t rows) {
+                return concat_group(context, count, weights, bytes, kd, ns, nullptr, outputs, rows, k, dev, true);
+            },
+            [&] { return concat_group(context, count, weights, bytes, kd, ns, a, outputs, m, k); });
+    }
     return concat_group(context, count, weights, bytes, kd, ns, a, outputs, m, k);
 }
 

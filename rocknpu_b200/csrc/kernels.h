@@ -99,6 +99,13 @@ int launch_gemm_tc(int kind, const void* w, long long ldw_bytes, const void* a, 
 void launch_gemv_w8a8(const int8_t* w, const float* w_scale, const int8_t* a8, const float* a_scale, int k, int n,
                       float* out, cudaStream_t s);
 
+// HILO two-part activations: residual rows res = x - dequant(quant(x)) of
+// each f32 row (non-finite -> *err), and the elementwise sum of the two
+// output halves.
+void launch_hilo_residual(const float* a, int m, int k, long long lda, float* res, long long ldr, int* err,
+                          cudaStream_t s);
+void launch_add_halves(const float* hi, const float* lo, float* out, long long len, cudaStream_t s);
+
 // SwiGLU between the M=1 gate/up and down projections.
 void launch_swiglu(const float* gate, const float* up, float* out, int n, cudaStream_t s);
 

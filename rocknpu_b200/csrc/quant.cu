@@ -298,6 +298,44 @@ __global__ void __launch_bounds__(kRowThreads) quant_rows_kernel(const float* __
     if (threadIdx.x == 0) scales[row] = scale;
 }
 
+// HILO (hilo_stack, capi/src/lib.rs:2045-2070): residual rows of the
+// two-part activation encoding, res = x - f32(q) * scale with q, scale from
+// the row's own quantisation (two f32 roundings, as the reference).
+__global__ void __launch_bounds__(kRowThreads) hilo_residual_kernel(const float* __restrict__ a, int k, long long lda,
+                                                                     float* __restrict__ res, long long ldr,
+                                                                     int* __restrict__ err) {
+    __shared__ float red[33];
+    const int row = blockIdx.x;
+    const float* src = a + static_cast<size_t>(row) * lda;
+    float amax = 0.0f;
+    bool finite = true;
+    for (int i = threadIdx.x; i < k; i += kRowThreads) {
+        const float v = src[i];
+        finite &= isfinite(v);
+        amax = fmaxf(amax, fabsf(v));
+    }
+    if (__syncthreads_or(!finite)) {
+        if (threadIdx.x == 0) atomicExch(err, kErrNonFinite);
+        return;
+    }
+    const float scale = row_scale(block_max(amax, red));
+    const float inv = row_inv(scale);
+    float* dst = res + static_cast<size_t>(row) * ldr;
+    for (int i = threadIdx.x; i < k; i += kRowThreads) {
+        const float x = src[i];
+        const float back = __fmul_rn(static_cast<float>(quant_value(x, scale, inv)), scale);
+        dst[i] = __fsub_rn(x, back);
+    }
+}
+
+// hilo_sum (capi/src/lib.rs:2073-2083): out = hi + lo, elementwise f32.
+__global__ void add_halves_kernel(const float* __restrict__ hi, const float* __restrict__ lo, float* __restrict__ out,
+                                  long long len) {
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < len; i += stride)
+        out[i] = __fadd_rn(hi[i], lo[i]);
+}
+
 __global__ void f32_to_f16_kernel(const float* __restrict__ a, int m, int k, long long lda, __half* __restrict__ out,
                                   long long ldo) {
     const long long total = static_cast<long long>(m) * k;
@@ -382,6 +420,16 @@ void launch_f32_to_f16(const float* a, int m, int k, long long lda, __half* out,
     const long long total = static_cast<long long>(m) * k;
     const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
     f32_to_f16_kernel<<<blocks, 256, 0, s>>>(a, m, k, lda, out, ldo);
+}
+
+void launch_hilo_residual(const float* a, int m, int k, long long lda, float* res, long long ldr, int* err,
+                          cudaStream_t s) {
+    hilo_residual_kernel<<<m, kRowThreads, 0, s>>>(a, k, lda, res, ldr, err);
+}
+
+void launch_add_halves(const float* hi, const float* lo, float* out, long long len, cudaStream_t s) {
+    const int blocks = static_cast<int>(std::min<long long>((len + 255) / 256, 148LL * 16));
+    add_halves_kernel<<<std::max(blocks, 1), 256, 0, s>>>(hi, lo, out, len);
 }
 
 void launch_swiglu(const float* gate, const float* up, float* out, int n, cudaStream_t s) {

@@ -390,3 +390,67 @@ def test_quantisers_round_like_the_ieee_quotient_near_half_integers(ctx, rng, mo
     dev.matmul_w8a8(ctx, torch.from_numpy(a).cuda(), torch.from_numpy(w8).cuda(), torch.from_numpy(ws).cuda(), out)
     assert rk.lib().rocknpu_b200_context_check(ctx.handle) == 0
     assert np.array_equal(_bits(out.cpu().numpy()), _bits(ref))
+
+
+# ---- HILO two-part activations (ROCKNPU_PREFILL_HILO) -------------------------
+
+def _prepared(kind, blocks, k, n):
+    st, w8, ws = oracle.prepare_w8a8(kind, blocks, k, n)
+    assert st == 0
+    return w8, ws
+
+
+@pytest.mark.parametrize("mode,kind,m,k,n", [("1", 4, 64, 2048, 512), ("all", 6, 33, 2048, 256),
+                                             ("down", 4, 16, 5632, 256), ("1", 4, 200, 2048, 2048)])
+def test_hilo_prompt_matches_oracle(ctx, rng, monkeypatch, mode, kind, m, k, n):
+    monkeypatch.setenv("ROCKNPU_PREFILL_HILO", mode)
+    blocks = rk.synth_q_weights(kind, n, k, seed=m + k)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    a[:, rng.choice(k, 20, replace=False)] *= 25.0
+    out = np.full((m, n), np.nan, dtype=np.float32)
+    assert ctx.matmul_q(kind, blocks, a, out, m, k, n) == 0
+    w8, ws = _prepared(kind, blocks, k, n)
+    st, ref = oracle.matmul_w8a8_hilo(w8, ws, a)
+    assert st == 0
+    assert np.array_equal(_bits(out), _bits(ref))
+    # it differs from the one-part encoding and is closer to the f32 product
+    st, plain = oracle.matmul_w8a8(w8, ws, a)
+    exact = a.astype(np.float64) @ (w8.astype(np.float64) * ws[:, None].astype(np.float64)).T
+    assert np.abs(ref - exact).max() < np.abs(plain - exact).max()
+
+
+def test_hilo_down_mode_leaves_narrow_k_alone(ctx, rng, monkeypatch):
+    m, k, n = 32, 2048, 256
+    blocks = rk.synth_q_weights(4, n, k, seed=9)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    monkeypatch.setenv("ROCKNPU_PREFILL_HILO", "down")
+    out = np.empty((m, n), dtype=np.float32)
+    assert ctx.matmul_q(4, blocks, a, out, m, k, n) == 0
+    w8, ws = _prepared(4, blocks, k, n)
+    st, ref = oracle.matmul_w8a8(w8, ws, a)
+    assert np.array_equal(_bits(out), _bits(ref))
+
+
+def test_hilo_concat_group_matches_oracle(ctx, rng, monkeypatch):
+    monkeypatch.setenv("ROCKNPU_PREFILL_HILO", "1")
+    m, k = 48, 2048
+    ns, kinds = [2048, 256, 256], [4, 4, 6]
+    ws = [rk.synth_q_weights(kd, n, k, seed=40 + i) for i, (kd, n) in enumerate(zip(kinds, ns))]
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    outs = [np.full((m, n), np.nan, dtype=np.float32) for n in ns]
+    assert ctx.matmul_q_concat(ws, kinds, ns, a, outs, m, k) == 0
+    for (kd, n, b, o) in zip(kinds, ns, ws, outs):
+        w8, s8 = _prepared(kd, b, k, n)
+        st, ref = oracle.matmul_w8a8_hilo(w8, s8, a)
+        assert np.array_equal(_bits(o), _bits(ref))
+
+
+def test_hilo_non_finite_takes_the_normal_path(ctx, rng, monkeypatch):
+    monkeypatch.setenv("ROCKNPU_PREFILL_HILO", "1")
+    m, k, n = 8, 512, 64
+    blocks = rk.synth_q_weights(4, n, k, seed=4)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    a[3, 7] = np.nan
+    out = np.zeros((m, n), dtype=np.float32)
+    assert ctx.matmul_q(4, blocks, a, out, m, k, n) == -1
+    assert not out.any()

@@ -160,3 +160,26 @@ def test_matmul_f16_oracle_is_f64_exact(rng):
     out = oracle.matmul_f16(w.view(np.uint16), a)
     ref = (a.astype(np.float16).astype(np.float64) @ w.astype(np.float64).T).astype(np.float32)
     assert np.allclose(out, ref, rtol=0, atol=1e-6)
+
+
+def test_hilo_stack_and_sum_restatement():
+    """hilo_stack (capi/src/lib.rs:2045-2070): [x; x - f32(q) * scale] with
+    q, scale from quantize_symmetric_into, in f32 without contraction; and
+    hilo_sum (:2073-2083).  The reference has no test of its own for these,
+    so the C oracle is checked against the same operations in numpy f32."""
+    rng = np.random.default_rng(5)
+    a = rng.standard_normal((9, 768)).astype(np.float32)
+    a[:, rng.choice(768, 8, replace=False)] *= 30.0
+    a[4] = 0.0
+    st, stacked = oracle.hilo_stack(a)
+    assert st == 0
+    st, q, s = oracle.quantize_rows(a)
+    back = (q.astype(np.float32) * s[:, None]).astype(np.float32)
+    residual = (a - back).astype(np.float32)
+    assert np.array_equal(stacked[:9].view(np.uint32), a.view(np.uint32))
+    assert np.array_equal(stacked[9:].view(np.uint32), residual.view(np.uint32))
+    halves = rng.standard_normal((2, 5, 7)).astype(np.float32)
+    assert np.array_equal(oracle.hilo_sum(halves.reshape(10, 7)), (halves[0] + halves[1]).astype(np.float32))
+    bad = a.copy()
+    bad[2, 3] = np.inf
+    assert oracle.hilo_stack(bad)[0] != 0
