@@ -1,6 +1,6 @@
 /*
  * rocknpu_b200.h -- what librocknpu.so adds beside the reference C ABI
- * (rocknpu.h).  Four groups:
+ * (rocknpu.h).  Five groups:
  *
  *  1. The ggml plugin's host rules (adapters/ggml-rocknpu), exported so a
  *     plugin built against ggml can call them and tests can check them
@@ -15,7 +15,8 @@
  *     (0 = ok, 1 = non-finite input, >1 = a device-side wait ran out).
  *  3. Multi-GPU N-sharding: the row split, the all-gather layout, and peer
  *     (CUDA IPC) buffers for a GEMM whose epilogue all-gathers over NVLink.
- *  4. Synthetic K-quant weights for tests and benchmarks (host only).
+ *  4. W8 sidecar files: the plugin's disk cache of prepared int8 weights.
+ *  5. Synthetic K-quant weights for tests and benchmarks (host only).
  */
 #ifndef ROCKNPU_B200_H
 #define ROCKNPU_B200_H
@@ -187,7 +188,33 @@ int rocknpu_b200_gemm_w8a8_gather(const int8_t *a_i8, size_t ld_a, const float *
                                   size_t ld_w, const float *w_scales, float *const *outs, size_t copies, size_t col0,
                                   size_t ldo, size_t m, size_t k, size_t n_local, int *status, rocknpu_stream stream);
 
-/* ---- 4. synthetic K-quant weights (host) ------------------------------- */
+/* ---- 4. W8 sidecar files (host) ---------------------------------------- */
+
+/* The plugin's disk cache of prepared weights (ggml-rocknpu.cpp:115-259,
+ * written by scripts/make_tinyllama_w8_sidecar_gguf.py): <dir>/<name>.w8
+ * (int8 [n][k]), <name>.scale.f32 (f32 [n]) and <name>.source.fnv1a64 (16 hex
+ * digits, the fingerprint below of the tensor's source bytes). */
+
+/* rocknpu_source_sample_fingerprint (ggml-rocknpu.cpp:123-146): FNV-1a 64
+ * over the source length (8 little-endian bytes), then the whole source when
+ * it is at most 12288 bytes, else three 4096-byte samples (start, middle,
+ * end). */
+uint64_t rocknpu_b200_source_fingerprint(const uint8_t *data, size_t bytes);
+
+/* Load a sidecar into host buffers (w8: k * n bytes, scales: n floats), as
+ * rocknpu_w8_sidecar_get does (ggml-rocknpu.cpp:212-243): OK when the
+ * fingerprint file matches `source`, both data files have exactly the
+ * expected size and every scale is finite and positive; otherwise
+ * ROCKNPU_STATUS_INVALID_ARGUMENT (the caller prepares the weight instead). */
+int rocknpu_b200_w8_sidecar_read(const char *dir, const char *name, const uint8_t *source, size_t source_bytes,
+                                 size_t k, size_t n, int8_t *w8, float *scales);
+
+/* Write the three sidecar files for prepared weights of `source` (creating
+ * `dir` if needed), byte-compatible with the reference script's output. */
+int rocknpu_b200_w8_sidecar_write(const char *dir, const char *name, const uint8_t *source, size_t source_bytes,
+                                  size_t k, size_t n, const int8_t *w8, const float *scales);
+
+/* ---- 5. synthetic K-quant weights (host) ------------------------------- */
 
 /* Deterministic N(0, sigma^2) f32 values (counter-based: value i depends only
  * on seed and i, so any slice can be generated independently). */

@@ -67,6 +67,8 @@ def lib():
         L.orc_matmul_f16.argtypes = [P, P, P, S, S, S]
         L.orc_swiglu.restype = None
         L.orc_swiglu.argtypes = [P, P, P, S]
+        L.orc_source_fingerprint.restype = ctypes.c_uint64
+        L.orc_source_fingerprint.argtypes = [P, S]
         L.orc_hilo_stack.restype = ctypes.c_int
         L.orc_hilo_stack.argtypes = [P, S, S, P]
         L.orc_hilo_sum.restype = None
@@ -176,6 +178,11 @@ def swiglu(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
     out = np.empty_like(gate)
     lib().orc_swiglu(_p(gate), _p(up), _p(out), gate.size)
     return out
+
+
+def source_fingerprint(data: np.ndarray) -> int:
+    data = np.ascontiguousarray(data, dtype=np.uint8).reshape(-1)
+    return int(lib().orc_source_fingerprint(_p(data), data.size))
 
 
 def hilo_stack(a: np.ndarray):

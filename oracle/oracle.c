@@ -389,6 +389,34 @@ void orc_hilo_sum(const float *stacked, size_t len, float *out) {
     for (size_t i = 0; i < len; ++i) out[i] = stacked[i] + stacked[len + i];
 }
 
+/* rocknpu_source_sample_fingerprint (adapters/ggml-rocknpu/src/
+ * ggml-rocknpu.cpp:123-146; the sidecar script's source_sample_fnv1a64):
+ * FNV-1a 64 over the length's 8 little-endian bytes, then all bytes up to
+ * 3 * 4096, else 4096-byte samples at 0, (len - 4096) / 2 and len - 4096. */
+uint64_t orc_source_fingerprint(const uint8_t *data, size_t bytes) {
+    const uint64_t prime = 1099511628211ULL;
+    uint64_t h = 14695981039346656037ULL;
+    for (unsigned shift = 0; shift < 64; shift += 8) {
+        h ^= (uint8_t)((uint64_t)bytes >> shift);
+        h *= prime;
+    }
+    size_t starts[3], counts[3], parts;
+    if (bytes <= 3 * 4096) {
+        starts[0] = 0; counts[0] = bytes; parts = 1;
+    } else {
+        starts[0] = 0; counts[0] = 4096;
+        starts[1] = (bytes - 4096) / 2; counts[1] = 4096;
+        starts[2] = bytes - 4096; counts[2] = 4096;
+        parts = 3;
+    }
+    for (size_t p = 0; p < parts; ++p)
+        for (size_t i = 0; i < counts[p]; ++i) {
+            h ^= data[starts[p] + i];
+            h *= prime;
+        }
+    return h;
+}
+
 /* split_blocks (rocknpu-matmul/src/int8_decode_pool.rs:1505-1522): an even
  * split of `blocks` blocks over `workers`, remainder to the first workers. */
 size_t orc_split_blocks(size_t blocks, size_t block_width, size_t workers, size_t *starts,

@@ -66,6 +66,8 @@ void orc_matmul_f16(const uint16_t *w_bits, const float *a, float *out, size_t m
 
 void orc_swiglu(const float *gate, const float *up, float *out, size_t n);
 
+uint64_t orc_source_fingerprint(const uint8_t *data, size_t bytes);
+
 int orc_hilo_stack(const float *a, size_t m, size_t k, float *stacked);
 void orc_hilo_sum(const float *stacked, size_t len, float *out);
 

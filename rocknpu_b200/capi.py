@@ -78,6 +78,9 @@ SIGNATURES = {
     "rocknpu_b200_peer_barrier": (_I, [_P, _P, _P]),
     "rocknpu_b200_peer_buffer_destroy": (None, [_P]),
     "rocknpu_b200_gemm_w8a8_gather": (_I, [_P, _S, _P, _P, _S, _P, _P, _S, _S, _S, _S, _S, _S, _P, _P]),
+    "rocknpu_b200_source_fingerprint": (ctypes.c_uint64, [_P, _S]),
+    "rocknpu_b200_w8_sidecar_read": (_I, [ctypes.c_char_p, ctypes.c_char_p, _P, _S, _S, _S, _P, _P]),
+    "rocknpu_b200_w8_sidecar_write": (_I, [ctypes.c_char_p, ctypes.c_char_p, _P, _S, _S, _S, _P, _P]),
     "rocknpu_synth_normal": (None, [ctypes.c_uint64, ctypes.c_uint64, _S, ctypes.c_float, _P]),
     "rocknpu_synth_encode": (_I, [_U32, _P, _S, _S, _P]),
 }

@@ -15,6 +15,13 @@ Outputs (all small, seeded, deterministic):
   (imported from the reference tree, run on the gguf-py dequantised rows).
   The plugin documents that sidecar as identical to its in-process
   conversion (ggml-rocknpu.cpp:160-163).
+* ``sidecar_fnv.npz`` -- the sampled FNV-1a-64 source fingerprints of the
+  W8 sidecar format, computed by the reference script's own
+  ``source_sample_fnv1a64`` (the plugin's rocknpu_source_sample_fingerprint,
+  ggml-rocknpu.cpp:123-146, must agree with it) for seeded byte arrays of
+  every size class (whole-array and three-sample cases), and the complete
+  sidecar files (``.w8``, ``.scale.f32``, ``.source.fnv1a64``) the script
+  writes for a small Q4_K and Q6_K tensor.
 * ``act_quant.npz`` -- the tie-heavy activation vector of the reference's
   quantisation test (capi/src/lib.rs:5680-5700: literal ties plus an LCG
   stream) with its int8 values and scale, computed here with an independent
@@ -78,8 +85,50 @@ def tie_vector() -> np.ndarray:
     return np.array(values, dtype=np.float32)
 
 
+def load_sidecar_script(ref_root: str):
+    spec = importlib.util.spec_from_file_location(
+        "rocknpu_sidecar", os.path.join(ref_root, "scripts", "make_tinyllama_w8_sidecar_gguf.py"))
+    sidecar = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(sidecar)
+    return sidecar
+
+
+FNV_SIZES = (1, 100, 4095, 4096, 12287, 12288, 12289, 13824, 30000, 100003)
+
+
+def fnv_fixture(ref_root: str) -> None:
+    from gguf import GGMLQuantizationType, dequantize
+    sidecar = load_sidecar_script(ref_root)
+    rng = np.random.default_rng(77)
+    out = {"sizes": np.array(FNV_SIZES, dtype=np.int64)}
+    hexes = []
+    for size in FNV_SIZES:
+        data = rng.integers(0, 256, size=size, dtype=np.uint8)
+        hexes.append(sidecar.source_sample_fnv1a64(data))
+    out["fnv_hex"] = np.array(hexes)
+    # whole sidecar files of two small tensors
+    for kind, qt in ((4, GGMLQuantizationType.Q4_K), (6, GGMLQuantizationType.Q6_K)):
+        n, k = 20, 512
+        blocks = random_kquant_blocks(kind, n * k // 256, rng)
+        rows = dequantize(blocks.reshape(-1), qt).astype(np.float32).reshape(n, k)
+        with tempfile.TemporaryDirectory() as tmp:
+            base = os.path.join(tmp, "blk.0.t.weight")
+            sidecar.quantize_rows(rows, __import__("pathlib").Path(base), 8)
+            out[f"q{kind}_blocks"] = blocks
+            out[f"q{kind}_w8_file"] = np.fromfile(base + ".w8", dtype=np.uint8)
+            out[f"q{kind}_scale_file"] = np.fromfile(base + ".scale.f32", dtype=np.uint8)
+            out[f"q{kind}_fnv_file"] = np.frombuffer(
+                (sidecar.source_sample_fnv1a64(blocks.reshape(-1)) + "\n").encode(), dtype=np.uint8)
+    np.savez_compressed(os.path.join(HERE, "sidecar_fnv.npz"), **out)
+
+
 def main() -> None:
     ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("ROCKNPU_REFERENCE", "")
+    if "--only" in sys.argv:
+        which = sys.argv[sys.argv.index("--only") + 1]
+        {"fnv": fnv_fixture}[which](ref_root)
+        print("wrote", which, "fixture to", HERE)
+        return
     from gguf import GGMLQuantizationType, dequantize
 
     rng = np.random.default_rng(20261201)
@@ -93,10 +142,7 @@ def main() -> None:
     np.savez_compressed(os.path.join(HERE, "kquant_dequant.npz"), **out)
 
     # W8 preparation through the reference's own sidecar quantiser.
-    spec = importlib.util.spec_from_file_location(
-        "rocknpu_sidecar", os.path.join(ref_root, "scripts", "make_tinyllama_w8_sidecar_gguf.py"))
-    sidecar = importlib.util.module_from_spec(spec)
-    spec.loader.exec_module(sidecar)
+    sidecar = load_sidecar_script(ref_root)
     w8 = {}
     n, k = 24, 1024
     for kind, qt in kinds.items():
@@ -123,6 +169,7 @@ def main() -> None:
     sr = np.array([quantize_symmetric_np(r)[1] for r in rows], dtype=np.float32)
     np.savez_compressed(os.path.join(HERE, "act_quant.npz"), ties=ties, ties_q=q,
                         ties_scale=np.array([s], dtype=np.float32), rows=rows, rows_q=qr, rows_scale=sr)
+    fnv_fixture(ref_root)
     print("wrote fixtures to", HERE)
 
 
