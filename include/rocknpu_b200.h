@@ -97,14 +97,20 @@ size_t rocknpu_b200_gemm_workspace_bytes(size_t m, size_t n, size_t k);
  * `workspace` (optional, device memory, all-zero before its first use; every
  * launch leaves it all-zero) lets short-M shapes split K across CTAs; NULL or
  * fewer than rocknpu_b200_gemm_workspace_bytes bytes runs without splits.
- * Launches that share a workspace must not overlap on the GPU. */
+ * Launches that share a workspace must not overlap on the GPU.
+ * The GEMM is a programmatic dependent launch: it starts streaming the
+ * weights (w_i8) before the preceding kernel on `stream` has finished, and
+ * reads everything else only after it.  So the weights must already be
+ * complete when the GEMM is queued (prepared in an earlier, synchronised
+ * step, as the context's caches do), not written by the kernel just before. */
 int rocknpu_b200_gemm_w8a8(const int8_t *a_i8, size_t ld_a, const float *a_scales, const int8_t *w_i8,
                            size_t ld_w, const float *w_scales, float *out, size_t ldo, int32_t *acc_out, size_t m,
                            size_t k, size_t n, void *workspace, size_t workspace_bytes, int *status,
                            rocknpu_stream stream);
 
 /* K2 + K3 (+ K5 for m == 1) through the context's workspace: the whole
- * W8A8 MUL_MAT on resident f32 activations and resident prepared weights. */
+ * W8A8 MUL_MAT on resident f32 activations and resident prepared weights
+ * (complete before the call: see rocknpu_b200_gemm_w8a8). */
 int rocknpu_b200_matmul_w8a8(rocknpu_context *context, const float *a, const int8_t *w_i8, const float *w_scales,
                              float *out, size_t m, size_t k, size_t n, rocknpu_stream stream);
 

@@ -355,6 +355,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *sh.tmem_slot;
+    // every CTA is resident: the next programmatic launch on the stream may
+    // start its prologue and weight prefetch on SMs as they free up (it reads
+    // anything this launch writes only after its own griddepcontrol.wait)
+    if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (warp == 0 || warp == 1) {
         if (lane == 0) {

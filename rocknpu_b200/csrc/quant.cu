@@ -258,7 +258,10 @@ __global__ void __launch_bounds__(kRowThreads) quant_rows_kernel(const float* __
     extern __shared__ __align__(16) float srow[];
     __shared__ float red[33];
     // let the dependent GEMM launch now: it sets up and streams weights while
-    // this kernel runs, and waits (griddepcontrol.wait) before reading our output
+    // this kernel runs, and waits (griddepcontrol.wait) before reading our
+    // output.  (This kernel is an ordinary launch: a programmatic one, waiting
+    // here for its own input, measured slower -- its waiting CTAs hold the
+    // shared memory the next GEMM's CTAs need.)
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int row = blockIdx.x;
     const float* src = a + static_cast<size_t>(row) * lda;
