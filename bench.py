@@ -22,6 +22,10 @@ weight cache), 1.0 GB per step > L2, so no extra L2 flush is needed.
   (oracle/, OpenMP, all host threads): per-token quantisation, int32 GEMM,
   rescale -- timed on a bounded sample of the same workload.
 
+Other configs: --workload llama32-1b (configs[2], pp512) and qwen25-1.5b
+(configs[3], pp2048) replay those models' MUL_MAT calls the same way;
+--workload cfg5 is the large-GEMM sharding sweep.
+
 Multi-GPU (torchrun): the path does not shard at this size, so each rank
 runs its own replica on its own prompt batch (weak scaling, no collective);
 value = all ranks' tokens / max-over-ranks time.
@@ -41,12 +45,38 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+# Shapes of the offloaded MUL_MATs of BASELINE.json configs[1..3] (the
+# query projection is hidden wide; kv = kv heads x head dim).
+MODELS = {
+    "tinyllama": dict(name="tinyllama-1.1b", layers=22, hidden=2048, ffn=5632, kv=256, tokens=512),
+    "llama32-1b": dict(name="llama-3.2-1b", layers=16, hidden=2048, ffn=8192, kv=512, tokens=512),
+    "qwen25-1.5b": dict(name="qwen2.5-1.5b", layers=28, hidden=1536, ffn=8960, kv=256, tokens=2048),
+}
+MODEL = "tinyllama"
 LAYERS = 22
 HIDDEN, FFN, KV = 2048, 5632, 256
 
 
+def set_model(name: str) -> None:
+    global MODEL, LAYERS, HIDDEN, FFN, KV
+    spec = MODELS[name]
+    MODEL = name
+    LAYERS, HIDDEN, FFN, KV = spec["layers"], spec["hidden"], spec["ffn"], spec["kv"]
+
+
+def workload_name(m: int) -> str:
+    return f"{MODELS[MODEL]['name']}-q4_k_m-prefill-pp{m}-mul_mat"
+
+
+def metric_name(m: int) -> str:
+    label = {"tinyllama": "TinyLlama", "llama32-1b": "Llama-3.2-1B", "qwen25-1.5b": "Qwen2.5-1.5B"}[MODEL]
+    return f"prefill tok/s pp{m} {label}-shape Q4_K_M (ggml MUL_MAT offload)"
+
+
 def layer_plan(layer: int):
-    """(name, [(kind, n)], k) of the four offloaded MUL_MAT calls of a layer."""
+    """(name, [(kind, n)], k) of the four offloaded MUL_MAT calls of a layer:
+    Q4_K everywhere except attn_v and every other ffn_down (Q6_K), as
+    llama.cpp's Q4_K_M mix places them."""
     down_kind = 6 if layer % 2 == 0 else 4
     return [("qkv", [(4, HIDDEN), (4, KV), (6, KV)], HIDDEN),
             ("o", [(4, HIDDEN)], HIDDEN),
@@ -105,7 +135,7 @@ def profiled_traffic(m: int):
     """DRAM bytes per step of the GEMM launches, from the committed ncu
     summary of this workload (profiles/gemm_tc_tinyllama_pp512_dram.md);
     None for token counts that were not captured."""
-    path = os.path.join(ROOT, "profiles", f"gemm_tc_tinyllama_pp{m}_dram.md")
+    path = os.path.join(ROOT, "profiles", f"gemm_tc_{MODEL}_pp{m}_dram.md")
     if not os.path.exists(path):
         return None
     with open(path) as f:
@@ -405,7 +435,7 @@ def run_ours(args, rank: int, world: int):
     if rank != 0:
         return None
     line = {
-        "metric": f"prefill tok/s pp{m} TinyLlama-shape Q4_K_M (ggml MUL_MAT offload)",
+        "metric": metric_name(m),
         "value": round(world * m / (ms * 1e-3), 1),
         "unit": "tok/s",
         "n_gpus": world,
@@ -417,7 +447,7 @@ def run_ours(args, rank: int, world: int):
         "vs_baseline": None,
         "dtype": "int8 (W8A8, int32 accumulate, f32 out)",
         "data": "synthetic (random-init N(0,0.02^2) -> Q4_K/Q6_K weights, N(0,1) activations)",
-        "config": {"workload": f"tinyllama-1.1b-q4_k_m-prefill-pp{m}-mul_mat", "tokens_per_step": m,
+        "config": {"workload": workload_name(m), "tokens_per_step": m,
                    "global_batch": world * m, "seq_len": m, "layers": LAYERS,
                    "calls_per_step": len(prepared), "parallelism": f"replicas{world}",
                    "l2": "inputs > L2: 0.97 GB resident int8 weights streamed per step"},
@@ -432,9 +462,15 @@ def run_ours(args, rank: int, world: int):
     return line
 
 
+# Token rows of the CPU samples: the CPU path's cost is linear in the rows,
+# so long prompts are timed on their first rows and scaled.
+CPU_SAMPLE_ROWS = 512
+
+
 def cpu_baseline(weights, acts, m, budget_s=20.0):
-    """The reference's CPU path (oracle C port, OpenMP) on whole calls of the
-    workload until the time budget is spent; scaled to tok/s of a step."""
+    """The reference's CPU path (oracle C port, OpenMP) on MUL_MAT calls of the
+    workload (the first CPU_SAMPLE_ROWS tokens of each) until the time budget
+    is spent; scaled by int8 ops to tok/s of a whole step."""
     import oracle
     prepared = []
     for key, blocks in list(weights.items())[:8]:  # two layers' worth of calls
@@ -448,11 +484,12 @@ def cpu_baseline(weights, acts, m, budget_s=20.0):
     calls = 0
     ops_done = 0
     t0 = time.perf_counter()
+    rows = min(m, CPU_SAMPLE_ROWS)
     while True:
         for key, w, s, k in prepared:
-            st, _ = oracle.matmul_w8a8(w, s, acts[key])
+            st, _ = oracle.matmul_w8a8(w, s, np.ascontiguousarray(acts[key][:rows]))
             calls += 1
-            ops_done += 2 * m * w.shape[0] * k
+            ops_done += 2 * rows * w.shape[0] * k
             if time.perf_counter() - t0 > budget_s:
                 break
         if time.perf_counter() - t0 > budget_s or calls >= 4 * len(prepared):
@@ -461,8 +498,8 @@ def cpu_baseline(weights, acts, m, budget_s=20.0):
     _, step_ops = algorithmic(m)
     step_s = dt * step_ops / ops_done
     return {"value": round(m / step_s, 2), "unit": "tok/s", "cores": oracle.threads(), "kind": "port",
-            "sample": f"{calls} whole MUL_MAT calls of layers 0-1 (quantize + int32 GEMM + rescale, "
-                      f"prepared weights), {dt:.1f} s, scaled by int8 ops to one 22-layer step"}
+            "sample": f"{calls} MUL_MAT calls of layers 0-1 on {rows} of {m} tokens (quantize + int32 GEMM + "
+                      f"rescale, prepared weights), {dt:.1f} s, scaled by int8 ops to one {LAYERS}-layer step"}
 
 
 def run_reference(args, rank: int, world: int):
@@ -484,7 +521,8 @@ def run_reference(args, rank: int, world: int):
             ws.append(w)
             ss.append(s)
         prepared.append((key, np.concatenate(ws), np.concatenate(ss), k))
-    # each step is a bounded sample: the calls of ONE layer, scaled to 22
+    # each step is a bounded sample: the calls of ONE layer, scaled to the
+    # model's layer count
     sample = prepared[:4]
 
     def step():
@@ -501,15 +539,15 @@ def run_reference(args, rank: int, world: int):
     value = round(m / step_s, 2)
     line = {
         "impl": "reference",
-        "metric": f"prefill tok/s pp{m} TinyLlama-shape Q4_K_M (ggml MUL_MAT offload)",
+        "metric": metric_name(m),
         "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(step_s * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int8 (W8A8, int32 accumulate, f32 out)", "data": "synthetic",
-        "config": {"workload": f"tinyllama-1.1b-q4_k_m-prefill-pp{m}-mul_mat", "tokens_per_step": m,
+        "config": {"workload": workload_name(m), "tokens_per_step": m,
                    "seq_len": m, "layers": LAYERS},
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": oracle.threads(), "kind": "port",
                          "sample": "each step times layer 0's four MUL_MAT calls (quantize + int32 GEMM + "
-                                   "rescale on prepared weights) and scales x22"},
+                                   f"rescale on prepared weights) and scales x{LAYERS}"},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     return line
@@ -656,15 +694,19 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--tokens", type=int, default=512)
+    ap.add_argument("--tokens", type=int, default=None, help="prompt tokens (default: the model's config)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
-    ap.add_argument("--workload", choices=["tinyllama", "cfg5"], default="tinyllama")
+    ap.add_argument("--workload", choices=list(MODELS) + ["cfg5"], default="tinyllama")
     ap.add_argument("--route", choices=["peer", "allgather"], default="peer",
                     help="cfg5 output exchange at N > 1")
     ap.add_argument("--m-list", default=",".join(str(m) for m in CFG5_M))
     args = ap.parse_args()
+    if args.workload in MODELS:
+        set_model(args.workload)
+        if args.tokens is None:
+            args.tokens = MODELS[args.workload]["tokens"]
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
