@@ -69,8 +69,7 @@ struct Cfg {
     static constexpr int kStage = kWBytes + kABytes;
     static constexpr int kBarOffset = STAGES * kStage;
     static constexpr int kNumBars = 2 * STAGES + 5;
-    static constexpr int kScaleOffset = kBarOffset + kNumBars * 8 + 32;  // 2 x 256 token scales
-    static constexpr int kBytes = kScaleOffset + 2 * 256 * 4 + 1024;      // + alignment slack
+    static constexpr int kBytes = kBarOffset + kNumBars * 8 + 32 + 1024;  // + alignment slack
     static constexpr uint32_t kTmemCols = 2 * kAcc * BT < 32 ? 32 : 2 * kAcc * BT;
     static_assert((kTmemCols & (kTmemCols - 1)) == 0 && kTmemCols <= 512, "TMEM allocation");
     static_assert(kBytes <= 232448, "shared memory");
@@ -85,18 +84,8 @@ struct Shared {
     uint32_t* tmem_slot;
     uint32_t* last_flag;
     volatile uint32_t* abort;
-    float* red;     // [kEpiWarps] cross-warp maxima of the fused quantiser
-    float* scales;  // [2][256] token scales of the epilogue's current unit
+    float* red;  // [kEpiWarps] cross-warp maxima of the fused quantiser
 };
-
-// Order later uses of registers filled by an asynchronous tcgen05.ld after
-// the tcgen05.wait::ld that completes it (the compiler sees no dependency
-// between the wait and the registers otherwise).
-__device__ __forceinline__ void reg_fence16(uint32_t (&r)[16]) {
-    asm volatile("" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
-                 "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),
-                 "+r"(r[14]), "+r"(r[15]));
-}
 
 __device__ __forceinline__ void fail(const GemmParams& p, const Shared& sh, int code) {
     atomicCAS(p.err, 0, code);
@@ -340,7 +329,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     sh.last_flag = sh.tmem_slot + 1;
     sh.abort = sh.tmem_slot + 2;
     sh.red = red;
-    sh.scales = reinterpret_cast<float*>(smem + C::kScaleOffset);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -515,38 +503,26 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                 if (ready && lane == 0) (void)ld_acquire_gpu(p.q_ready + t.m0 / BT);
                 __syncwarp();
             }
-            // this unit's token scales, staged once in shared memory (double
-            // buffered by unit parity; the barrier below is reached by every
-            // epilogue warp for every unit, so the buffer a warp overwrites
-            // was released by all of them one unit earlier)
-            float* ssc = sh.scales + (j & 1) * 256;
-            if constexpr (KIND == 0) {
-                if (!split) {
-                    for (int i = etid; i < BT; i += kEpiWarps * 32) {
-                        const int m = t.m0 + i;
-                        ssc[i] = (ready && m < p.m) ? load_scale<MODE>(p.a_scale + m) : 0.0f;
-                    }
-                }
-                epilogue_bar();
-            }
             if (ready) {
                 tc_fence_after();
+                const float* __restrict__ a_scale = p.a_scale;
                 int32_t* __restrict__ acc_out = p.acc_out;
                 int32_t* __restrict__ wsp = p.ws;
-                // chunks of 16 token columns; the TMEM load of chunk i + 1 is
-                // in flight while chunk i is rescaled and stored
-                constexpr int kChunks = C::kAcc == 2 ? BT / 16 : (BT + 31) / 32;
-                uint32_t ra[16], rb[16];
-                if (c_first < BT) tmem_ld16(lane_base + c_first, ra);
+#pragma unroll 1
+                for (int c = c_first; c < BT; c += c_step) {
+                    // the chunk's token scales, loaded before any store of
+                    // the chunk (stores could otherwise order every load)
+                    float asv[16];
+                    if constexpr (KIND == 0) {
 #pragma unroll
-                for (int ci = 0; ci < kChunks; ++ci) {
-                    const int c = c_first + ci * c_step;
-                    if (c >= BT) break;  // warp-uniform
-                    uint32_t(&r)[16] = (ci & 1) ? rb : ra;
-                    uint32_t(&nxt)[16] = (ci & 1) ? ra : rb;
+                        for (int jj = 0; jj < 16; ++jj) {
+                            const int m = t.m0 + c + jj;
+                            asv[jj] = (!split && m < p.m) ? load_scale<MODE>(a_scale + m) : 0.0f;
+                        }
+                    }
+                    uint32_t r[16];
+                    tmem_ld16(lane_base + c, r);
                     tmem_ld_wait();
-                    reg_fence16(r);
-                    if (ci + 1 < kChunks && c + c_step < BT) tmem_ld16(lane_base + c + c_step, nxt);
                     if (col_ok) {
                         float* __restrict__ o = out + static_cast<long long>(t.m0 + c) * ldo + ocol;
 #pragma unroll
@@ -557,8 +533,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                                     if (split) {
                                         atomicAdd(wsp + static_cast<long long>(m) * p.n + col, static_cast<int>(r[jj]));
                                     } else {
-                                        const float v = __fmul_rn(
-                                            __fmul_rn(__int2float_rn(static_cast<int>(r[jj])), ssc[c + jj]), wsc);
+                                        const float v =
+                                            __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[jj])), asv[jj]), wsc);
                                         if constexpr (MODE == kGather) {
                                             const long long off = static_cast<long long>(m) * ldo + ocol;
 #pragma unroll 1
