@@ -554,6 +554,147 @@ def run_reference(args, rank: int, world: int):
 
 
 # ---------------------------------------------------------------------------
+# FP16-executor variant (configs[3]: "the same GEMMs with fp16 weights")
+# ---------------------------------------------------------------------------
+
+def f16_calls():
+    """(layer, name, member index, n, k) of every FP16-executor call of a step:
+    each member of the model's MUL_MATs is one rocknpu_matmul_f16_f32_f32."""
+    out = []
+    for layer in range(LAYERS):
+        for name, members, k in layer_plan(layer):
+            for i, (_, n) in enumerate(members):
+                out.append((layer, name, i, n, k))
+    return out
+
+
+def run_ours_f16(args, rank: int, world: int):
+    """The model's MUL_MATs through the FP16 executor (K4, tcgen05 kind::f16):
+    f16 weights ~ N(0, 0.02^2), f32 activations converted to f16 per call."""
+    import torch
+    import oracle
+    import rocknpu_b200 as rk
+    from rocknpu_b200 import device as dev
+
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+    m = args.tokens
+    hbm_peak, bf16_peak, peak_src = load_peaks()
+    calls = f16_calls()
+    t0 = time.time()
+    w_host, a_host = {}, {}
+    for idx, (layer, name, i, n, k) in enumerate(calls):
+        w_host[idx] = rk.synth_normal(3000 + idx, n * k, 0.02).astype(np.float16).reshape(n, k)
+    for layer in range(LAYERS):
+        for name, _, k in layer_plan(layer):
+            a_host[(layer, name)] = rk.synth_normal(5000 + 97 * rank + len(a_host), m * k).reshape(m, k)
+    gen_s = time.time() - t0
+    status = dev.new_status()
+    w_dev = {idx: torch.from_numpy(w).cuda() for idx, w in w_host.items()}
+    a_dev = {key: torch.from_numpy(a).cuda() for key, a in a_host.items()}
+    a16 = {key: torch.empty(a.shape, dtype=torch.float16, device="cuda") for key, a in a_dev.items()}
+    outs = {}
+    for idx, (layer, name, i, n, k) in enumerate(calls):
+        outs.setdefault((name, i), torch.empty((m, n), dtype=torch.float32, device="cuda"))
+
+    def step():
+        for key in a_dev:
+            dev.convert_f16(a_dev[key], out=a16[key])
+        for idx, (layer, name, i, n, k) in enumerate(calls):
+            dev.gemm_f16(a16[(layer, name)], w_dev[idx], status, out=outs[(name, i)])
+
+    def gemm_only():
+        for idx, (layer, name, i, n, k) in enumerate(calls):
+            dev.gemm_f16(a16[(layer, name)], w_dev[idx], status, out=outs[(name, i)])
+
+    def graph_time(fn, reps):
+        fn()
+        torch.cuda.synchronize()
+        g = new_graph()
+        with torch.cuda.graph(g):
+            fn()
+        for _ in range(args.warmup):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps, graph_kernel_nodes(g)
+
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        clocks.mark("t_start")
+        ms, launches = graph_time(step, args.steps)
+        clocks.mark("t_end")
+    gemm_ms, _ = graph_time(gemm_only, max(5, args.steps))
+    assert status.item() == 0
+    flops = sum(2 * m * n * k for (_, _, _, n, k) in calls)
+    byts = sum(2 * n * k + 2 * m * k + 4 * m * n for (_, _, _, n, k) in calls)
+    tf = flops / (gemm_ms * 1e-3) / 1e12
+    gbs = byts / (gemm_ms * 1e-3) / 1e9
+    bound = "tensor" if flops / (bf16_peak * 1e12) >= byts / (hbm_peak * 1e9) else "hbm"
+    roof = {"bound": bound, "achieved": round(tf if bound == "tensor" else gbs, 1),
+            "peak": bf16_peak if bound == "tensor" else hbm_peak, "unit": "TFLOP/s" if bound == "tensor" else "GB/s",
+            "frac": round(tf / bf16_peak if bound == "tensor" else gbs / hbm_peak, 4), "traffic": None,
+            "kernel": "gemm_tc_kernel (K4, tcgen05 kind::f16)", "peak_source": f"{peak_src} bf16_tflops / hbm_gbs",
+            "tensor_frac": round(tf / bf16_peak, 4), "hbm_frac": round(gbs / hbm_peak, 4),
+            "gemm_ms_per_step": round(gemm_ms, 4), "gemm_launches_per_step": len(calls)}
+    e2e = None
+    if not args.no_e2e:
+        ctx = rk.Context()
+        h_a = {key: torch.from_numpy(a).pin_memory() for key, a in a_host.items()}
+        h_w = {idx: w.view(np.uint16) for idx, w in w_host.items()}
+        h_o = {}
+        for (_, name, i, n, _) in calls:
+            h_o.setdefault((name, i), torch.empty((m, n), dtype=torch.float32).pin_memory())
+
+        def e2e_step():
+            for idx, (layer, name, i, n, k) in enumerate(calls):
+                st = ctx.matmul_f16(h_w[idx], h_a[(layer, name)].numpy(), h_o[(name, i)].numpy(), m, k, n)
+                if st != 0:
+                    raise RuntimeError(f"rocknpu_matmul_f16_f32_f32 failed: {st}")
+        e2e_step()
+        t1 = time.perf_counter()
+        e_steps = max(1, min(args.steps, 5))
+        for _ in range(e_steps):
+            e2e_step()
+        e2e_s = (time.perf_counter() - t1) / e_steps
+        h2d = sum(4 * m * k for (_, _, _, n, k) in calls)
+        d2h = sum(4 * m * n for (_, _, _, n, k) in calls)
+        e2e = {"value": round(m / e2e_s, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "ms_per_step": round(e2e_s * 1e3, 3), "path": "rocknpu_matmul_f16_f32_f32 per member, pinned host"}
+        ctx.close()
+    cpu = None
+    if not args.no_cpu_baseline:
+        rows = min(m, 128)
+        t1 = time.perf_counter()
+        done = 0
+        sample = [c for c in enumerate(calls)][:7]
+        for idx, (layer, name, i, n, k) in sample:
+            oracle.matmul_f16(w_host[idx].view(np.uint16), np.ascontiguousarray(a_host[(layer, name)][:rows]))
+            done += 2 * rows * n * k
+            if time.perf_counter() - t1 > args.cpu_seconds:
+                break
+        dt = time.perf_counter() - t1
+        cpu = {"value": round(m / (dt * flops / done), 3), "unit": "tok/s", "cores": oracle.threads(), "kind": "port",
+               "sample": f"FP16 oracle (f64 accumulation, lib.rs:1680-1699) on {rows} tokens of layer 0's calls, "
+                         f"{dt:.1f} s, scaled by flops to one {LAYERS}-layer step"}
+    return {
+        "metric": metric_name(m).replace("Q4_K_M", "FP16-executor"),
+        "value": round(m / (ms * 1e-3), 1), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16 (f32 accumulate, f32 out)",
+        "data": "synthetic (random-init N(0,0.02^2) f16 weights, N(0,1) activations)",
+        "config": {"workload": workload_name(m).replace("q4_k_m", "f16"), "tokens_per_step": m, "layers": LAYERS,
+                   "calls_per_step": len(calls), "parallelism": "replicas1"},
+        "roofline": roof, "e2e": e2e, "cpu_baseline": cpu,
+        "gpu_launches": launches * args.steps if launches is not None else None, "launches_per_step": launches,
+        "clocks": clocks.summary(), "setup_s": round(gen_s, 1),
+    }
+
+
+# ---------------------------------------------------------------------------
 # cfg5: the large-GEMM sharding sweep (BASELINE.json configs[4])
 # ---------------------------------------------------------------------------
 
@@ -702,6 +843,7 @@ def main():
     ap.add_argument("--route", choices=["peer", "allgather"], default="peer",
                     help="cfg5 output exchange at N > 1")
     ap.add_argument("--m-list", default=",".join(str(m) for m in CFG5_M))
+    ap.add_argument("--f16", action="store_true", help="model workloads through the FP16 executor (one GPU)")
     args = ap.parse_args()
     if args.workload in MODELS:
         set_model(args.workload)
@@ -722,6 +864,8 @@ def main():
             line = run_reference(args, rank, world)
         elif args.workload == "cfg5":
             line = run_cfg5(args, rank, world)
+        elif args.f16:
+            line = run_ours_f16(args, rank, world) if rank == 0 else None
         else:
             line = run_ours(args, rank, world)
     finally:

@@ -138,6 +138,12 @@ int rocknpu_b200_matmul_w8a8(rocknpu_context *context, const float *a, const int
 int rocknpu_b200_matmul_w8a8_noalloc(const float *a, const int8_t *w_i8, const float *w_scales, float *out,
                                      size_t m, size_t k, size_t n, int *status, rocknpu_stream stream);
 
+/* The FP16 executor's activation conversion (Fp16MatmulExecutor::execute_f32,
+ * rocknpu-matmul/src/lib.rs:251): f32 a[m][lda] -> f16 out[m][ldo], round to
+ * nearest even; columns k..ldo of out are left as they are. */
+int rocknpu_b200_convert_f16(const float *a, size_t m, size_t k, size_t lda, uint16_t *out, size_t ldo,
+                             rocknpu_stream stream);
+
 /* K4: out[m][ldo] = sum_k f16(a)[m][k] * w_f16[n][k] in f32 on tcgen05;
  * a_f16 row pitch ld_a elements (multiple of 8). */
 int rocknpu_b200_gemm_f16(const uint16_t *a_f16, size_t ld_a, const uint16_t *w_f16, size_t ld_w, float *out,

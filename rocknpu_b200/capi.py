@@ -68,6 +68,7 @@ SIGNATURES = {
     "rocknpu_b200_gemm_w8a8": (_I, [_P, _S, _P, _P, _S, _P, _P, _S, _P, _S, _S, _S, _P, _S, _P, _P]),
     "rocknpu_b200_matmul_w8a8": (_I, [_P, _P, _P, _P, _P, _S, _S, _S, _P]),
     "rocknpu_b200_matmul_w8a8_noalloc": (_I, [_P, _P, _P, _P, _S, _S, _S, _P, _P]),
+    "rocknpu_b200_convert_f16": (_I, [_P, _S, _S, _S, _P, _S, _P]),
     "rocknpu_b200_gemm_f16": (_I, [_P, _S, _P, _S, _P, _S, _S, _S, _S, _P, _P]),
     "rocknpu_b200_gemv_w8a8": (_I, [_P, _P, _P, _P, _P, _S, _S, _P]),
     "rocknpu_b200_shard_rows": (_S, [_S, _S, _P, _P]),

@@ -1296,6 +1296,14 @@ int rocknpu_b200_matmul_w8a8(rocknpu_context* context, const float* a, const int
     return e == cudaSuccess ? kOk : kExecError;
 }
 
+int rocknpu_b200_convert_f16(const float* a, size_t m, size_t k, size_t lda, uint16_t* out, size_t ldo,
+                             rocknpu_stream stream) {
+    if (!a || !out || m == 0 || k == 0 || lda < k || ldo < k || m > 0x7fffffff || k > 0x7fffffff) return kInvalid;
+    rk::launch_f32_to_f16(a, static_cast<int>(m), static_cast<int>(k), static_cast<long long>(lda),
+                          reinterpret_cast<__half*>(out), static_cast<long long>(ldo), static_cast<cudaStream_t>(stream));
+    return cuda_status(cudaGetLastError());
+}
+
 int rocknpu_b200_gemm_f16(const uint16_t* a_f16, size_t ld_a, const uint16_t* w_f16, size_t ld_w, float* out,
                           size_t ldo, size_t m, size_t k, size_t n, int* status, rocknpu_stream stream) {
     if (!a_f16 || !w_f16 || !out || !status || m == 0 || k == 0 || n == 0 || ld_a < k || ld_w < k || ldo < n ||

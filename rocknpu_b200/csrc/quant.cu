@@ -339,13 +339,25 @@ __global__ void add_halves_kernel(const float* __restrict__ hi, const float* __r
         out[i] = __fadd_rn(hi[i], lo[i]);
 }
 
+// Rows strided over the grid, 4 values per thread step when the rows are
+// 16-byte (f32) / 8-byte (f16) aligned.
 __global__ void f32_to_f16_kernel(const float* __restrict__ a, int m, int k, long long lda, __half* __restrict__ out,
-                                  long long ldo) {
-    const long long total = static_cast<long long>(m) * k;
-    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const long long r = i / k, c = i % k;
-        out[r * ldo + c] = __float2half_rn(a[r * lda + c]);
+                                  long long ldo, bool vec) {
+    for (int r = blockIdx.x; r < m; r += gridDim.x) {
+        const float* src = a + static_cast<long long>(r) * lda;
+        __half* dst = out + static_cast<long long>(r) * ldo;
+        if (vec) {
+            for (int c = threadIdx.x * 4; c < k; c += blockDim.x * 4) {
+                const float4 v = __ldg(reinterpret_cast<const float4*>(src + c));
+                __half2 lo = __floats2half2_rn(v.x, v.y), hi = __floats2half2_rn(v.z, v.w);
+                uint2 w;
+                w.x = *reinterpret_cast<uint32_t*>(&lo);
+                w.y = *reinterpret_cast<uint32_t*>(&hi);
+                *reinterpret_cast<uint2*>(dst + c) = w;
+            }
+        } else {
+            for (int c = threadIdx.x; c < k; c += blockDim.x) dst[c] = __float2half_rn(src[c]);
+        }
     }
 }
 
@@ -420,9 +432,10 @@ void launch_quant_rows(const float* a, int m, int k, long long lda, int8_t* a8, 
 }
 
 void launch_f32_to_f16(const float* a, int m, int k, long long lda, __half* out, long long ldo, cudaStream_t s) {
-    const long long total = static_cast<long long>(m) * k;
-    const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
-    f32_to_f16_kernel<<<blocks, 256, 0, s>>>(a, m, k, lda, out, ldo);
+    const bool vec = k % 4 == 0 && lda % 4 == 0 && ldo % 4 == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(out) & 7) == 0;
+    const int blocks = std::max(1, std::min(m, 148 * 8));
+    f32_to_f16_kernel<<<blocks, 256, 0, s>>>(a, m, k, lda, out, ldo, vec);
 }
 
 void launch_hilo_residual(const float* a, int m, int k, long long lda, float* res, long long ldr, int* err,

@@ -73,6 +73,16 @@ def gemm_w8a8(a8: torch.Tensor, a_scales: torch.Tensor, w8: torch.Tensor, w_scal
     return out
 
 
+def convert_f16(a: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """The FP16 executor's f32 -> f16 activation conversion (round to nearest even)."""
+    assert a.is_cuda and a.dtype == torch.float32 and a.dim() == 2 and a.stride(1) == 1
+    m, k = a.shape
+    out = torch.empty((m, k), dtype=torch.float16, device=a.device) if out is None else out
+    _check(lib().rocknpu_b200_convert_f16(a.data_ptr(), m, k, a.stride(0), out.data_ptr(), out.stride(0),
+                                          _stream(stream)), "convert_f16")
+    return out
+
+
 def gemm_f16(a16: torch.Tensor, w16: torch.Tensor, status: torch.Tensor, out: torch.Tensor | None = None,
              stream=None):
     """K4: f16 [m, k] . f16 [n, k]^T accumulated in f32."""

@@ -454,3 +454,13 @@ def test_hilo_non_finite_takes_the_normal_path(ctx, rng, monkeypatch):
     out = np.zeros((m, n), dtype=np.float32)
     assert ctx.matmul_q(4, blocks, a, out, m, k, n) == -1
     assert not out.any()
+
+
+@pytest.mark.parametrize("m,k,lda", [(3, 100, 100), (64, 2048, 2048), (7, 96, 128)])
+def test_convert_f16_rounds_to_nearest_even(dev, rng, m, k, lda):
+    a = (rng.standard_normal((m, lda)) * 1000).astype(np.float32)
+    a[0, :4] = [65520.0, -65519.0, 5.96e-8, 2.0 ** -25]  # overflow to inf, near-max, subnormal, tie to zero
+    ta = torch.from_numpy(a).cuda()[:, :k]
+    out = dev.convert_f16(ta)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy().view(np.uint16), a[:, :k].astype(np.float16).view(np.uint16))
