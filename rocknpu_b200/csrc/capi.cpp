@@ -399,12 +399,19 @@ struct OutSeg {
 // Chunks carry at least ~1.5 MB in their larger direction -- smaller copies
 // lose PCIe bandwidth to per-copy cost -- and there are at most kMaxChunks.
 size_t chunk_rows(size_t m, size_t k, size_t total_n) {
+    // tuning override, results unchanged: ROCKNPU_B200_CHUNK_ROWS (multiple of 16)
+    if (const char* v = std::getenv("ROCKNPU_B200_CHUNK_ROWS")) {
+        const size_t r = static_cast<size_t>(std::atol(v));
+        if (r >= 16 && r % 16 == 0) return std::min(m, std::max(r, (m + RockNpuContext::kMaxChunks - 1) /
+                                                                       RockNpuContext::kMaxChunks));
+    }
+    // >= ~2 MB per copy and >= 128 rows per chunk: measured on B200 at
+    // m = 512 for the TinyLlama calls, smaller chunks lose more to per-copy
+    // and per-launch latency than they gain in overlap
     const size_t row_bytes = std::max(k, total_n) * sizeof(float);
-    const size_t min_rows = std::max<size_t>(16, ((size_t(3) << 19) + row_bytes - 1) / row_bytes);
-    size_t rows = std::max(min_rows, (m + 7) / 8);
+    size_t rows = std::max<size_t>(128, ((size_t(2) << 20) + row_bytes - 1) / row_bytes);
     rows = std::max(rows, (m + RockNpuContext::kMaxChunks - 1) / RockNpuContext::kMaxChunks);
-    rows = std::max<size_t>(round_up(rows, 16), 64);  // m <= 64: one chunk
-    return std::min(m, rows);
+    return std::min(m, round_up(rows, 16));
 }
 
 // Quantisation + GEMM (GEMV for m == 1) of host activations against a
