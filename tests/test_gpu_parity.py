@@ -145,6 +145,34 @@ def test_gemm_w8a8_int32_exact(dev, rng, m, k, n, split):
         assert not ws.any().item()
 
 
+@pytest.mark.parametrize("wt,bt", [(128, 256), (256, 128), (128, 128), (256, 64), (128, 16), (256, 16)])
+@pytest.mark.parametrize("m,k,n", [(300, 1024, 640), (512, 2048, 2560), (257, 384, 300), (1000, 640, 1024)])
+def test_gemm_every_tile_configuration_exact(dev, rng, monkeypatch, wt, bt, m, k, n):
+    """The tile plan is a heuristic; every instantiated configuration (forced
+    through the tuning overrides) must give the same bits, with ragged M, N
+    and K edges."""
+    monkeypatch.setenv("ROCKNPU_B200_GEMM_WT", str(wt))
+    monkeypatch.setenv("ROCKNPU_B200_GEMM_BT", str(bt))
+    a8 = rng.integers(-127, 128, size=(m, k), dtype=np.int8)
+    w8 = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
+    a_s = rng.uniform(0.001, 0.1, size=m).astype(np.float32)
+    w_s = rng.uniform(0.001, 0.1, size=n).astype(np.float32)
+    acc_ref = oracle.gemm_i8_i32(a8, w8)
+    status = dev.new_status()
+    ta8, tas, tw8, tws = (torch.from_numpy(x).cuda() for x in (a8, a_s, w8, w_s))
+    for _ in range(2):  # two launches: units reuse the accumulator buffers
+        acc = torch.full((m, n), -7, dtype=torch.int32, device="cuda")
+        out = dev.gemm_w8a8(ta8, tas, tw8, tws, status, acc=acc)
+        torch.cuda.synchronize()
+        assert status.item() == 0
+        assert np.array_equal(acc.cpu().numpy(), acc_ref)
+    exp = np.empty((m, n), dtype=np.float32)
+    for r in range(m):
+        oracle.lib().orc_rescale_i32_row(oracle._p(np.ascontiguousarray(acc_ref[r])), oracle._p(w_s),
+                                         float(a_s[r]), oracle._p(exp[r]), n)
+    assert np.array_equal(_bits(out.cpu().numpy()), _bits(exp))
+
+
 @pytest.mark.parametrize("m", [4, 8, 12, 16, 32, 48, 64, 128])
 def test_gemm_mtile_kat(dev, m):
     # crates/rocket-smoke/src/bin/int8_mtile.rs:28-86
