@@ -235,7 +235,73 @@ int orc_prepare_w8a8(uint32_t kind, const uint8_t *bytes, size_t nbytes, size_t 
  * of rocket-smoke/src/bin/int8_decode_m1.rs:38-45).  Sums use wrapping int32
  * like the K-split host accumulation (capi/src/lib.rs:1906-1914); for
  * |x| <= 127 and K <= 2^17 no wrap occurs. */
+#if defined(__x86_64__)
+#include <immintrin.h>
+
+/* The same exact product with AVX-512 VNNI (the CPU baseline's fast path):
+ * vpdpbusd multiplies unsigned by signed bytes, so A is offset to a + 128
+ * (a ^ 0x80) and 128 * sum_k w[j][k] is subtracted afterwards -- exact in
+ * int32 for |values| <= 127 and k <= 2^17.  4 x 4 output tiles, 64 bytes of
+ * K per step; masked loads cover the K tail (masked W bytes are zero, so the
+ * offset A bytes there multiply to zero). */
+__attribute__((target("avx512f,avx512bw,avx512vnni")))
+static void gemm_vnni(const int8_t *a, const int8_t *w, int32_t *c, size_t m, size_t k, size_t n) {
+    int32_t *wsum = (int32_t *)malloc(n * sizeof(int32_t));
+#pragma omp parallel for schedule(static)
+    for (long j = 0; j < (long)n; ++j) {
+        int32_t t = 0;
+        for (size_t kk = 0; kk < k; ++kk) t += w[(size_t)j * k + kk];
+        wsum[j] = t;
+    }
+    const long rb = (long)((m + 3) / 4), cb = (long)((n + 3) / 4);
+    const __m512i flip = _mm512_set1_epi8((char)0x80);
+#pragma omp parallel for schedule(dynamic, 4) collapse(2)
+    for (long jb = 0; jb < cb; ++jb) {
+        for (long ib = 0; ib < rb; ++ib) {
+            const int8_t *ar[4], *wr[4];
+            for (int t = 0; t < 4; ++t) {
+                size_t i = (size_t)ib * 4 + t, j = (size_t)jb * 4 + t;
+                ar[t] = a + (i < m ? i : m - 1) * k;
+                wr[t] = w + (j < n ? j : n - 1) * k;
+            }
+            __m512i acc[4][4];
+            for (int x = 0; x < 4; ++x)
+                for (int y = 0; y < 4; ++y) acc[x][y] = _mm512_setzero_si512();
+            for (size_t kk = 0; kk < k; kk += 64) {
+                const size_t left = k - kk;
+                const __mmask64 mask = left >= 64 ? ~(__mmask64)0 : (((__mmask64)1 << left) - 1);
+                __m512i va[4], vw[4];
+                for (int t = 0; t < 4; ++t) {
+                    va[t] = _mm512_xor_si512(_mm512_maskz_loadu_epi8(mask, ar[t] + kk), flip);
+                    vw[t] = _mm512_maskz_loadu_epi8(mask, wr[t] + kk);
+                }
+                for (int x = 0; x < 4; ++x)
+                    for (int y = 0; y < 4; ++y) acc[x][y] = _mm512_dpbusd_epi32(acc[x][y], va[x], vw[y]);
+            }
+            for (int x = 0; x < 4; ++x) {
+                const size_t i = (size_t)ib * 4 + x;
+                if (i >= m) continue;
+                for (int y = 0; y < 4; ++y) {
+                    const size_t j = (size_t)jb * 4 + y;
+                    if (j >= n) continue;
+                    c[i * n + j] = _mm512_reduce_add_epi32(acc[x][y]) - 128 * wsum[j];
+                }
+            }
+        }
+    }
+    free(wsum);
+}
+#endif
+
 void orc_gemm_i8_i32(const int8_t *a, const int8_t *w, int32_t *c, size_t m, size_t k, size_t n) {
+#if defined(__x86_64__)
+    const char *force = getenv("ORACLE_SCALAR_GEMM");
+    if ((!force || force[0] != '1') && k <= ((size_t)1 << 17) && __builtin_cpu_supports("avx512f") &&
+        __builtin_cpu_supports("avx512bw") && __builtin_cpu_supports("avx512vnni")) {
+        gemm_vnni(a, w, c, m, k, n);
+        return;
+    }
+#endif
     const size_t NB = 16;
 #pragma omp parallel for schedule(dynamic, 1) collapse(2)
     for (long nb = 0; nb < (long)((n + NB - 1) / NB); ++nb) {
