@@ -16,8 +16,9 @@ weight cache), 1.0 GB per step > L2, so no extra L2 flush is needed.
 * value: tok/s with activations already in HBM (device entry point
   rocknpu_b200_matmul_w8a8 per MUL_MAT: K2 per-token quantisation + the K3
   tcgen05 W8A8 GEMM, launched programmatically after it).
-* e2e:   tok/s through the reference C ABI with pinned host buffers, as the
-  plugin calls it (rocknpu_matmul_q_concat_f32_f32_mtile for the groups,
+* e2e:   tok/s through the reference C ABI with page-locked host buffers
+  (rocknpu_b200_host_alloc), as the plugin calls it
+  (rocknpu_matmul_q_concat_f32_f32_mtile for the groups,
   rocknpu_matmul_q{4,6}_k_f32_f32 for O and down): H2D of every activation
   and D2H of every output inside the timed region.
 * cpu_baseline / --impl reference: the reference's CPU path restated in C
@@ -39,7 +40,6 @@ import json
 import os
 import statistics
 import sys
-import threading
 import time
 
 import numpy as np
@@ -156,9 +156,28 @@ def load_peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+_SAMPLER_SRC = r"""
+import sys, time
+import pynvml
+pynvml.nvmlInit()
+h = pynvml.nvmlDeviceGetHandleByIndex(int(sys.argv[1]))
+getr = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+out = open(sys.argv[2], "w")
+out.write("max %d\n" % pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+out.flush()
+while True:
+    t = time.monotonic()
+    out.write("%.6f %d %d\n" % (t, pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM), getr(h)))
+    out.flush()
+    time.sleep(0.002)
+"""
+
+
 class ClockSampler:
     """SM clocks and clock-event (throttle) reasons sampled through NVML every
-    2 ms during the timed region (nvidia-smi as a fallback)."""
+    2 ms during the timed region, by a separate process (a sampling thread
+    here could starve while the timed loop holds the interpreter lock);
+    timestamps are CLOCK_MONOTONIC, shared by both processes."""
 
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
                0x80: "hw_power_brake_slowdown"}
@@ -167,48 +186,71 @@ class ClockSampler:
         self.cuda_index = cuda_index
         self.samples = []  # (time, sm MHz, reason bits)
         self.max_mhz = None
-        self._stop = threading.Event()
 
-    def _handle(self):
-        import pynvml
+    def _read(self):
+        try:
+            with open(self.path) as f:
+                lines = f.read().splitlines()
+        except OSError:
+            return
+        samples = []
+        for line in lines:
+            parts = line.split()
+            if len(parts) == 2 and parts[0] == "max":
+                self.max_mhz = int(parts[1])
+            elif len(parts) == 3:
+                samples.append((float(parts[0]), int(parts[1]), int(parts[2])))
+        self.samples = samples
+
+    def __enter__(self):
+        import subprocess
+        import tempfile
         import torch
-        pynvml.nvmlInit()
         try:
             idx = torch.cuda._get_nvml_device_index(self.cuda_index)
         except Exception:
             idx = self.cuda_index
-        return pynvml, pynvml.nvmlDeviceGetHandleByIndex(idx)
-
-    def _run(self):
-        try:
-            nv, h = self._handle()
-            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
-            getr = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or nv.nvmlDeviceGetCurrentClocksThrottleReasons
-            while not self._stop.is_set():
-                t = time.perf_counter()
-                mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
-                r = getr(h)
-                self.samples.append((t, mhz, r))
-                time.sleep(0.002)
-        except Exception as exc:  # no NVML: leave the record empty but say why
-            self.error = repr(exc)
-
-    def __enter__(self):
-        self.thread = threading.Thread(target=self._run, daemon=True)
-        self.thread.start()
-        time.sleep(0.05)
+        fd, self.path = tempfile.mkstemp(prefix="rocknpu_clocks_", suffix=".txt")
+        os.close(fd)
+        self.proc = subprocess.Popen([sys.executable, "-c", _SAMPLER_SRC, str(idx), self.path],
+                                     stdout=subprocess.DEVNULL, stderr=subprocess.PIPE)
+        # wait for the first samples (the sampler imports NVML first)
+        deadline = time.monotonic() + 20.0
+        while time.monotonic() < deadline and self.proc.poll() is None:
+            self._read()
+            if len(self.samples) >= 2:
+                break
+            time.sleep(0.01)
+        if self.proc.poll() is not None:
+            self.error = self.proc.stderr.read().decode(errors="replace").strip()[-300:] or "sampler exited"
         return self
 
     def __exit__(self, *exc):
-        self._stop.set()
-        self.thread.join(timeout=5)
+        time.sleep(0.005)  # one more sample after the region
+        if self.proc.poll() is None:
+            self.proc.terminate()
+        try:
+            self.proc.wait(timeout=10)
+        except Exception:
+            self.proc.kill()
+        self._read()
+        try:
+            os.remove(self.path)
+        except OSError:
+            pass
 
     def mark(self, name):
-        setattr(self, name, time.perf_counter())
+        setattr(self, name, time.monotonic())
 
     def summary(self):
         t0, t1 = getattr(self, "t_start", None), getattr(self, "t_end", None)
         win = [x for x in self.samples if (t0 is None or x[0] >= t0) and (t1 is None or x[0] <= t1)]
+        if not win and t0 is not None and t1 is not None:
+            # a region shorter than the sampling period: the samples just
+            # before and after it
+            before = [x for x in self.samples if x[0] < t0][-1:]
+            after = [x for x in self.samples if x[0] > t1][:1]
+            win = before + after
         reasons = set()
         for _, _, r in win:
             for bit, name in self.REASONS.items():
@@ -423,20 +465,25 @@ def run_ours(args, rank: int, world: int):
                  "gemm_launches_per_step": len(prepared),
                  "algorithmic_bytes_per_step": alg_bytes, "int8_ops_per_step": alg_ops})
 
-    # e2e through the reference C ABI with pinned host buffers
+    # e2e through the reference C ABI with page-locked host buffers
     e2e = None
     if not args.no_e2e:
-        h_acts = {key: torch.from_numpy(a).pin_memory() for key, a in acts.items()}
+        # page-locked host buffers from the library's allocator (huge-page
+        # backed: steady host-to-device copy rate)
+        h_acts = {}
+        for key, a in acts.items():
+            h_acts[key] = rk.host_empty(a.shape)
+            h_acts[key][...] = a
         h_outs = {}
         for key in prepared:
             members = layer_plan(key[0])[["qkv", "o", "gate_up", "down"].index(key[1])][1]
-            h_outs[key] = [torch.empty((m, n), dtype=torch.float32).pin_memory() for _, n in members]
+            h_outs[key] = [rk.host_empty((m, n)) for _, n in members]
 
         def e2e_step():
             for key, blocks in weights.items():
                 _, members, k = layer_plan(key[0])[["qkv", "o", "gate_up", "down"].index(key[1])]
-                a = h_acts[key].numpy()
-                os_ = [o.numpy() for o in h_outs[key]]
+                a = h_acts[key]
+                os_ = h_outs[key]
                 if len(members) > 1:
                     st = ctx.matmul_q_concat(blocks, [kd for kd, _ in members], [n for _, n in members], a, os_, m, k)
                 else:
@@ -459,7 +506,8 @@ def run_ours(args, rank: int, world: int):
         h2d, d2h = h2d_d2h_bytes(m)
         e2e = {"value": round(world * m / e2e_s, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_s * 1e3, 3),
-               "path": "rocknpu_matmul_q_concat_f32_f32_mtile + rocknpu_matmul_q{4,6}_k_f32_f32, pinned host"}
+               "path": "rocknpu_matmul_q_concat_f32_f32_mtile + rocknpu_matmul_q{4,6}_k_f32_f32, "
+                       "rocknpu_b200_host_alloc host buffers"}
 
     if dist is not None:
         t = torch.tensor([ms], device="cuda")
@@ -507,7 +555,7 @@ def run_ours(args, rank: int, world: int):
 CPU_SAMPLE_ROWS = 512
 
 
-def cpu_baseline(weights, acts, m, budget_s=20.0):
+def cpu_baseline(weights, acts, m, budget_s=10.0):
     """The reference's CPU path (oracle C port, OpenMP) on MUL_MAT calls of the
     workload (the first CPU_SAMPLE_ROWS tokens of each) until the time budget
     is spent; scaled by int8 ops to tok/s of a whole step."""
@@ -532,7 +580,7 @@ def cpu_baseline(weights, acts, m, budget_s=20.0):
             ops_done += 2 * rows * w.shape[0] * k
             if time.perf_counter() - t0 > budget_s:
                 break
-        if time.perf_counter() - t0 > budget_s or calls >= 4 * len(prepared):
+        if time.perf_counter() - t0 > budget_s:
             break
     dt = time.perf_counter() - t0
     _, step_ops = algorithmic(m)
@@ -561,12 +609,10 @@ def run_reference(args, rank: int, world: int):
             ws.append(w)
             ss.append(s)
         prepared.append((key, np.concatenate(ws), np.concatenate(ss), k))
-    # each step is a bounded sample: the calls of ONE layer, scaled to the
-    # model's layer count
-    sample = prepared[:4]
-
+    # each step is the whole workload: every layer's MUL_MAT calls over all
+    # m tokens (quantize + exact int32 GEMM + rescale, VNNI, all host threads)
     def step():
-        for key, w, s, k in sample:
+        for key, w, s, k in prepared:
             oracle.matmul_w8a8(w, s, acts[key])
 
     for _ in range(args.warmup):
@@ -574,8 +620,7 @@ def run_reference(args, rank: int, world: int):
     t0 = time.perf_counter()
     for _ in range(args.steps):
         step()
-    layer_s = (time.perf_counter() - t0) / args.steps
-    step_s = layer_s * LAYERS
+    step_s = (time.perf_counter() - t0) / args.steps
     value = round(m / step_s, 2)
     line = {
         "impl": "reference",
@@ -586,8 +631,8 @@ def run_reference(args, rank: int, world: int):
         "config": {"workload": workload_name(m), "tokens_per_step": m,
                    "seq_len": m, "layers": LAYERS},
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": oracle.threads(), "kind": "port",
-                         "sample": "each step times layer 0's four MUL_MAT calls (quantize + int32 GEMM + "
-                                   f"rescale on prepared weights) and scales x{LAYERS}"},
+                         "sample": f"each step runs all {len(prepared)} MUL_MAT calls of the {LAYERS} layers on "
+                                   f"{m} tokens (quantize + int32 GEMM + rescale on prepared weights)"},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     return line
@@ -683,15 +728,19 @@ def run_ours_f16(args, rank: int, world: int):
     e2e = None
     if not args.no_e2e:
         ctx = rk.Context()
-        h_a = {key: torch.from_numpy(a).pin_memory() for key, a in a_host.items()}
+        h_a = {}
+        for key, a in a_host.items():
+            h_a[key] = rk.host_empty(a.shape)
+            h_a[key][...] = a
         h_w = {idx: w.view(np.uint16) for idx, w in w_host.items()}
         h_o = {}
         for (_, name, i, n, _) in calls:
-            h_o.setdefault((name, i), torch.empty((m, n), dtype=torch.float32).pin_memory())
+            if (name, i) not in h_o:
+                h_o[(name, i)] = rk.host_empty((m, n))
 
         def e2e_step():
             for idx, (layer, name, i, n, k) in enumerate(calls):
-                st = ctx.matmul_f16(h_w[idx], h_a[(layer, name)].numpy(), h_o[(name, i)].numpy(), m, k, n)
+                st = ctx.matmul_f16(h_w[idx], h_a[(layer, name)], h_o[(name, i)], m, k, n)
                 if st != 0:
                     raise RuntimeError(f"rocknpu_matmul_f16_f32_f32 failed: {st}")
         e2e_step()
@@ -703,7 +752,7 @@ def run_ours_f16(args, rank: int, world: int):
         h2d = sum(4 * m * k for (_, _, _, n, k) in calls)
         d2h = sum(4 * m * n for (_, _, _, n, k) in calls)
         e2e = {"value": round(m / e2e_s, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "ms_per_step": round(e2e_s * 1e3, 3), "path": "rocknpu_matmul_f16_f32_f32 per member, pinned host"}
+               "ms_per_step": round(e2e_s * 1e3, 3), "path": "rocknpu_matmul_f16_f32_f32 per member, rocknpu_b200_host_alloc host buffers"}
         ctx.close()
     cpu = None
     if not args.no_cpu_baseline:

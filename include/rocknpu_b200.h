@@ -73,6 +73,32 @@ typedef void *rocknpu_stream;
 /* The context's own stream. */
 rocknpu_stream rocknpu_b200_context_stream(rocknpu_context *context);
 
+/* 1 when the host-pointer entry points of include/rocknpu.h access the host
+ * range [ptr, ptr + bytes) in place instead of copying it: the range lies in
+ * one page-locked allocation mapped into the device's address space at its
+ * host address (cudaHostAlloc / cudaMallocHost memory).  Then the quantiser
+ * (or the FP16 conversion) reads the activations over PCIe and the GEMM
+ * epilogue stores the outputs there, overlapping the transfers with the
+ * tiles -- when ROCKNPU_B200_ZERO_COPY is "1" (both), "in" or "out"; unset or
+ * "0", every host buffer takes the chunked copy pipeline, which measured
+ * faster on B200.  0 for pageable memory, which is always copied.  The
+ * results are the same bits either way.  An output accessed in place
+ * stays untouched when the call is rejected (a non-finite activation), as
+ * a copied one does. */
+int rocknpu_b200_host_mapped(const void *ptr, size_t bytes);
+
+/* Page-locked host memory for the host-pointer entry points' activations and
+ * outputs: `bytes` rounded up to 2 MB, 2 MB-aligned, backed by transparent
+ * huge pages where the kernel provides them, registered with CUDA (portable,
+ * device-mapped).  Host-to-device copies out of it run at the link rate at
+ * every size, where copies out of 4 KB-page pinned memory vary widely.
+ * NULL when the memory cannot be mapped or registered (e.g. no GPU). */
+void *rocknpu_b200_host_alloc(size_t bytes);
+
+/* Release a rocknpu_b200_host_alloc buffer; INVALID_ARGUMENT for any other
+ * pointer.  No copy from or to it may still be in flight. */
+int rocknpu_b200_host_free(void *ptr);
+
 /* Wait for the context's stream and turn its device status word (written by
  * rocknpu_b200_matmul_w8a8) into a status code, clearing it. */
 int rocknpu_b200_context_check(rocknpu_context *context);

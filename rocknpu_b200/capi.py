@@ -62,6 +62,9 @@ SIGNATURES = {
     "rocknpu_mul_mat_supported": (_I, [_P]),
     "rocknpu_b200_context_stream": (_P, [_P]),
     "rocknpu_b200_context_check": (_I, [_P]),
+    "rocknpu_b200_host_mapped": (_I, [_P, _S]),
+    "rocknpu_b200_host_alloc": (_P, [_S]),
+    "rocknpu_b200_host_free": (_I, [_P]),
     "rocknpu_b200_prepare_w8": (_I, [_U32, _P, _S, _S, _P, _P, _P, _P]),
     "rocknpu_b200_quantize_rows": (_I, [_P, _S, _S, _P, _S, _P, _P, _P]),
     "rocknpu_b200_gemm_workspace_bytes": (_S, [_S, _S, _S]),
@@ -128,6 +131,34 @@ def ptr(a):
         return None
     assert a.flags["C_CONTIGUOUS"], "buffers must be C-contiguous"
     return a.ctypes.data_as(ctypes.c_void_p)
+
+
+class _HostBlock:
+    """Owner of one rocknpu_b200_host_alloc buffer, released with the object;
+    numpy views of it keep it alive through their ``base``."""
+
+    def __init__(self, nbytes: int):
+        p = lib().rocknpu_b200_host_alloc(nbytes)
+        if not p:
+            raise RuntimeError(f"rocknpu_b200_host_alloc({nbytes}) failed (no GPU, or the memory cannot be locked)")
+        self.ptr = p
+        self.__array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (p, False), "version": 3}
+
+    def __del__(self):
+        p, self.ptr = getattr(self, "ptr", None), None
+        if p and _lib is not None:
+            _lib.rocknpu_b200_host_free(p)
+
+
+def host_empty(shape, dtype=np.float32) -> np.ndarray:
+    """Uninitialised host array in rocknpu_b200_host_alloc memory (page-locked,
+    huge-page backed): the buffer type for the host-pointer entry points'
+    activations and outputs."""
+    dtype = np.dtype(dtype)
+    shape = (shape,) if isinstance(shape, int) else tuple(shape)
+    nbytes = int(np.prod(shape, dtype=np.int64)) * dtype.itemsize
+    raw = np.asarray(_HostBlock(max(nbytes, 1)))
+    return raw[:nbytes].view(dtype).reshape(shape)
 
 
 def device_count() -> int:

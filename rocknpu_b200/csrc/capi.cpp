@@ -7,6 +7,8 @@
 // per context.  All arithmetic runs in the sm_100a kernels (kernels.h);
 // there is no CPU compute path.  Citations are file:line in the
 // darkautism/RockNPU tree; "L" is crates/rocknpu-capi/src/lib.rs.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -17,6 +19,7 @@
 #include <cstring>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <set>
 #include <unordered_map>
 #include <vector>
@@ -269,6 +272,10 @@ struct RockNpuContext {
     bool profile = false;
     size_t mtile_calls = 0, mtile_hits = 0, mtile_misses = 0;
     uint64_t mtile_ns = 0, prepare_ns = 0;
+    // host-pointer W8A8 pipeline phases: queueing every chunk's copies and
+    // launches, then waiting for the kernels (+ status word), then for the
+    // last output copy
+    uint64_t issue_ns = 0, compute_wait_ns = 0, copy_wait_ns = 0;
 
     rocknpu_overlap_fn overlap = nullptr;
     void* overlap_user = nullptr;
@@ -312,9 +319,9 @@ int reset_status(Ctx* c) { return cuda_status(cudaMemsetAsync(c->d_status, 0, si
 // own launch.  Returns a cudaError_t value.
 int launch_w8a8(Ctx* c, const int8_t* w, const float* w_scales, const float* a_dev, size_t m, size_t k, size_t n,
                 int8_t* a8, size_t ld8, float* as, const rk::OutMembers& om, const rk::GemmWorkspace* gws,
-                cudaStream_t s) {
+                cudaStream_t s, bool allow_fused = true) {
     const int mi = static_cast<int>(m), ki = static_cast<int>(k), ni = static_cast<int>(n);
-    if (rk::fused_quant_enabled(mi, ki) && reinterpret_cast<uintptr_t>(a_dev) % 16 == 0) {
+    if (allow_fused && rk::fused_quant_enabled(mi, ki) && reinterpret_cast<uintptr_t>(a_dev) % 16 == 0) {
         const size_t elems = rk::fused_quant_sync_elems(mi, ni, ki);
         if (c->quant_sync.ensure(elems * sizeof(unsigned)) != cudaSuccess) return cudaErrorMemoryAllocation;
         rk::FusedQuant fq;
@@ -414,9 +421,65 @@ size_t chunk_rows(size_t m, size_t k, size_t total_n) {
     return std::min(m, round_up(rows, 16));
 }
 
+PFN_cuPointerGetAttributes_v7000 pointer_attributes_fn() {
+    static PFN_cuPointerGetAttributes_v7000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void* f = nullptr;
+        if (cudaGetDriverEntryPointByVersion("cuPointerGetAttributes", &f, 7000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuPointerGetAttributes_v7000>(f);
+    });
+    return fn;
+}
+
+// True when kernels may read and write the host range [p, p + bytes) at the
+// same address: the whole range lies in one page-locked host allocation that
+// is mapped into the device's address space at its host address (memory from
+// cudaHostAlloc / cudaMallocHost under unified addressing; not pageable
+// memory, not write-combined or separately mapped registrations).
+bool host_mapped(const void* p, size_t bytes) {
+    PFN_cuPointerGetAttributes_v7000 fn = pointer_attributes_fn();
+    if (fn == nullptr || p == nullptr || bytes == 0) return false;
+    CUpointer_attribute attrs[4] = {CU_POINTER_ATTRIBUTE_MEMORY_TYPE, CU_POINTER_ATTRIBUTE_DEVICE_POINTER,
+                                    CU_POINTER_ATTRIBUTE_RANGE_START_ADDR, CU_POINTER_ATTRIBUTE_RANGE_SIZE};
+    unsigned int type = 0;
+    CUdeviceptr dptr = 0, start = 0;
+    size_t size = 0;
+    void* data[4] = {&type, &dptr, &start, &size};
+    const CUdeviceptr addr = reinterpret_cast<CUdeviceptr>(p);
+    // cuPointerGetAttributes reports unknown (pageable) pointers as type 0
+    // without an error; any failure also means "not mapped"
+    if (fn(4, attrs, data, addr) != CUDA_SUCCESS) return false;
+    return type == CU_MEMORYTYPE_HOST && dptr == addr && size != 0 && start <= addr && addr - start <= size &&
+           bytes <= size - (addr - start);
+}
+
+// Direct host access for host-pointer calls (ROCKNPU_B200_ZERO_COPY; results
+// are identical either way): "1" = inputs and outputs, "in", "out", "0" or
+// unset = neither (copies through device buffers).  Only buffers for which
+// host_mapped() holds are accessed directly; others are copied.  Off by
+// default: on B200 over PCIe 5 the copy engines move the TinyLlama calls'
+// rows faster (gate/up group at m = 512: 520 us copied, 568 us in place)
+// than the kernels' own 128-byte loads and stores to host memory.
+void zero_copy_mode(bool* in, bool* out) {
+    const char* v = std::getenv("ROCKNPU_B200_ZERO_COPY");
+    if (v != nullptr && !std::strcmp(v, "1")) {
+        *in = *out = true;
+    } else {
+        *in = v != nullptr && !std::strcmp(v, "in");
+        *out = v != nullptr && !std::strcmp(v, "out");
+    }
+}
+
 // Quantisation + GEMM (GEMV for m == 1) of host activations against a
 // resident int8 weight, member outputs copied back, pipelined over row
-// chunks on three streams.  On INVALID_ARGUMENT (a non-finite activation)
+// chunks on three streams.  Page-locked, device-mapped host buffers are not
+// copied: the quantiser reads the activation rows from host memory and the
+// GEMM epilogue stores the outputs into host memory, so the transfers overlap
+// the compute tile by tile.  On INVALID_ARGUMENT (a non-finite activation)
 // output rows of chunks that were already copied back hold their results.
 // With `dev_a` the activations are already in device memory (one chunk, no
 // copy in), and with `keep` the outputs stay in c->out_f32 (member i's
@@ -488,34 +551,47 @@ int run_w8a8(Ctx* c, const PreparedW8& pw, const float* host_a, size_t m, size_t
         return cuda_status(cudaStreamSynchronize(c->stream));
     }
 
+    const uint64_t t_issue = c->profile ? now_ns() : 0;
+    bool zin = false, zout = false;
+    zero_copy_mode(&zin, &zout);
+    zin = zin && host_mapped(host_a, m * k * sizeof(float));
+    for (size_t i = 0; i < nseg && zout; ++i) zout = host_mapped(segs[i].host, m * segs[i].n * sizeof(float));
+
     rk::GemmWorkspace gws;
-    const size_t rows = chunk_rows(m, k, total_n);
+    // with both sides in host memory the whole call is one launch pair
+    const size_t rows = zin && zout ? m : chunk_rows(m, k, total_n);
     // the pipeline reuses one split-K workspace per chunk: size it for the
-    // largest chunk (stream order keeps chunk launches from overlapping)
-    if (context_ws(c, rows, total_n, k, &gws) != kOk) return kExecError;
+    // largest chunk (stream order keeps chunk launches from overlapping);
+    // direct host outputs run without K splits (the epilogue's store guard
+    // does not cover the split-K fixup)
+    if (!zout && context_ws(c, rows, total_n, k, &gws) != kOk) return kExecError;
     int chunk = 0;
     for (size_t r0 = 0; r0 < m; r0 += rows, ++chunk) {
         const size_t mr = std::min(rows, m - r0);
         cudaEvent_t ein = c->ev_in[chunk % RockNpuContext::kMaxChunks];
         cudaEvent_t eout = c->ev_out[chunk % RockNpuContext::kMaxChunks];
         if (chunk >= RockNpuContext::kMaxChunks) return kExecError;  // chunk_rows bounds the count
-        if (cudaMemcpyAsync(a_dev + r0 * k, host_a + r0 * k, mr * k * sizeof(float), cudaMemcpyHostToDevice, c->h2d) ||
-            cudaEventRecord(ein, c->h2d) || cudaStreamWaitEvent(c->stream, ein, 0))
+        const float* a_src = zin ? host_a + r0 * k : a_dev + r0 * k;
+        if (!zin && (cudaMemcpyAsync(a_dev + r0 * k, host_a + r0 * k, mr * k * sizeof(float), cudaMemcpyHostToDevice,
+                                     c->h2d) ||
+                     cudaEventRecord(ein, c->h2d) || cudaStreamWaitEvent(c->stream, ein, 0)))
             return kExecError;
         rk::OutMembers om;
         om.count = static_cast<int>(nseg);
+        om.store_guard = zout;
         size_t start = 0;
         for (size_t i = 0; i < nseg; ++i) {
             om.n_start[i] = static_cast<int>(start);
-            om.out[i] = out + m * start + r0 * segs[i].n;
+            om.out[i] = zout ? segs[i].host + r0 * segs[i].n : out + m * start + r0 * segs[i].n;
             om.ldo[i] = static_cast<long long>(segs[i].n);
             start += segs[i].n;
         }
         om.n_start[nseg] = static_cast<int>(start);
-        const int e = launch_w8a8(c, pw.w, pw.scales, a_dev + r0 * k, mr, k, total_n, a8 + r0 * ld8, ld8, as + r0, om,
-                                  &gws, c->stream);
-        if (e != cudaSuccess || cudaEventRecord(eout, c->stream) || cudaStreamWaitEvent(c->d2h, eout, 0))
-            return kExecError;
+        const int e = launch_w8a8(c, pw.w, pw.scales, a_src, mr, k, total_n, a8 + r0 * ld8, ld8, as + r0, om,
+                                  zout ? nullptr : &gws, c->stream, /*allow_fused=*/!zout);
+        if (e != cudaSuccess) return kExecError;
+        if (zout) continue;  // the epilogue stored this chunk's rows in place
+        if (cudaEventRecord(eout, c->stream) || cudaStreamWaitEvent(c->d2h, eout, 0)) return kExecError;
         if (rows >= m) {
             // one chunk: check the status first so a rejected call leaves
             // the caller's output untouched, as the reference does
@@ -530,8 +606,15 @@ int run_w8a8(Ctx* c, const PreparedW8& pw, const float* host_a, size_t m, size_t
             start += segs[i].n;
         }
     }
+    const uint64_t t_wait = c->profile ? now_ns() : 0;
     st = finish(c);
+    const uint64_t t_done = c->profile ? now_ns() : 0;
     const int st2 = cuda_status(cudaStreamSynchronize(c->d2h));
+    if (c->profile) {
+        c->issue_ns += t_wait - t_issue;
+        c->compute_wait_ns += t_done - t_wait;
+        c->copy_wait_ns += now_ns() - t_done;
+    }
     return st != kOk ? st : st2;
 }
 
@@ -546,22 +629,31 @@ int run_f16(Ctx* c, const PreparedF16& pw, const float* host_a, size_t m, size_t
         return kExecError;
     int st = reset_status(c);
     if (st != kOk) return st;
-    if (!dev_a &&
+    // page-locked, device-mapped host buffers are read / written in place
+    bool zin = false, zout = false;
+    if (!dev_a) {
+        zero_copy_mode(&zin, &zout);
+        zin = zin && host_mapped(host_a, m * k * sizeof(float));
+        zout = zout && !keep && host_mapped(host_out, m * n * sizeof(float));
+    }
+    if (!dev_a && !zin &&
         cudaMemcpyAsync(c->a_f32.ptr, host_a, m * k * sizeof(float), cudaMemcpyHostToDevice, c->stream))
         return kExecError;
-    rk::launch_f32_to_f16(dev_a ? dev_a : c->a_f32.as<float>(), static_cast<int>(m), static_cast<int>(k),
-                          static_cast<long long>(k), c->a_f16.as<__half>(), static_cast<long long>(ldh), c->stream);
+    rk::launch_f32_to_f16(dev_a ? dev_a : zin ? host_a : c->a_f32.as<float>(), static_cast<int>(m),
+                          static_cast<int>(k), static_cast<long long>(k), c->a_f16.as<__half>(),
+                          static_cast<long long>(ldh), c->stream);
     rk::OutMembers om;
     om.count = 1;
     om.n_start[1] = static_cast<int>(n);
-    om.out[0] = c->out_f32.as<float>();
+    om.out[0] = zout ? host_out : c->out_f32.as<float>();
     om.ldo[0] = static_cast<long long>(n);
+    om.store_guard = zout;
     const int e = rk::launch_gemm_tc(1, pw.w, static_cast<long long>(pw.ld * 2), c->a_f16.ptr,
                                      static_cast<long long>(ldh * 2), static_cast<int>(m), static_cast<int>(n),
                                      static_cast<int>(k), nullptr, nullptr, om, nullptr, 0, c->d_status, c->stream);
     if (e != cudaSuccess) return kExecError;
     st = finish(c);
-    if (st != kOk || keep) return st;
+    if (st != kOk || keep || zout) return st;
     if (cudaMemcpyAsync(host_out, c->out_f32.ptr, m * n * sizeof(float), cudaMemcpyDeviceToHost, c->stream))
         return kExecError;
     return cuda_status(cudaStreamSynchronize(c->stream));
@@ -804,6 +896,7 @@ int quant_kind46(uint32_t kind) { return kind == 4 ? rk::kQ4K : kind == 6 ? rk::
 int concat_group(Ctx* c, size_t count, const uint8_t* const* weights, const size_t* bytes, const int* kinds,
                  const size_t* ns, const float* a, float* const* outs, size_t m, size_t k, const float* dev_a = nullptr,
                  bool keep = false) {
+    const uint64_t t0 = c->profile ? now_ns() : 0;
     KeyList keys;
     std::vector<Member> members;
     std::vector<OutSeg> segs;
@@ -824,7 +917,12 @@ int concat_group(Ctx* c, size_t count, const uint8_t* const* weights, const size
     } else {
         c->mtile_hits++;
     }
-    return run_w8a8(c, *it->second, a, m, k, segs.data(), count, false, dev_a, keep);
+    const int st = run_w8a8(c, *it->second, a, m, k, segs.data(), count, false, dev_a, keep);
+    if (c->profile) {
+        c->mtile_calls++;
+        c->mtile_ns += now_ns() - t0;
+    }
+    return st;
 }
 
 
@@ -907,8 +1005,9 @@ void rocknpu_context_destroy(rocknpu_context* context) {
     if (c->profile) {
         std::fprintf(stderr,
                      "ROCKNPU MTILE PROFILE calls=%zu cache_hits=%zu cache_misses=%zu total_ms=%.3f "
-                     "weight_prepare_ms=%.3f\n",
-                     c->mtile_calls, c->mtile_hits, c->mtile_misses, c->mtile_ns / 1e6, c->prepare_ns / 1e6);
+                     "weight_prepare_ms=%.3f issue_ms=%.3f compute_wait_ms=%.3f copy_wait_ms=%.3f\n",
+                     c->mtile_calls, c->mtile_hits, c->mtile_misses, c->mtile_ns / 1e6, c->prepare_ns / 1e6,
+                     c->issue_ns / 1e6, c->compute_wait_ns / 1e6, c->copy_wait_ns / 1e6);
     }
     c->mtile.clear();
     c->groups.clear();
@@ -1224,6 +1323,8 @@ int rocknpu_matmul_w8a8_swiglu_down_f32(rocknpu_context* context, const int8_t* 
 rocknpu_stream rocknpu_b200_context_stream(rocknpu_context* context) {
     return context ? static_cast<rocknpu_stream>(context->stream) : nullptr;
 }
+
+int rocknpu_b200_host_mapped(const void* ptr, size_t bytes) { return host_mapped(ptr, bytes) ? 1 : 0; }
 
 int rocknpu_b200_context_check(rocknpu_context* context) {
     if (!context) return kInvalid;

@@ -217,8 +217,9 @@ int launch_gemm_tc(int kind, const void* w, long long ldw_bytes, const void* a, 
     if (outs.copies < 1 || outs.copies > kMaxCopies || (outs.copies > 1 && outs.count != 1))
         return cudaErrorInvalidValue;
     GemmPlan pl = plan_gemm(kind, m, n, k);
-    if (pl.ksplit > 1 && (outs.copies > 1 || ws == nullptr || ws->ws == nullptr || ws->counters == nullptr ||
-                          ws->ws_elems < pl.ws_elems || ws->counter_elems < pl.counter_elems)) {
+    if (pl.ksplit > 1 && (outs.copies > 1 || outs.store_guard || ws == nullptr || ws->ws == nullptr ||
+                          ws->counters == nullptr || ws->ws_elems < pl.ws_elems ||
+                          ws->counter_elems < pl.counter_elems)) {
         // no (large enough) workspace: one unit per tile over the whole K
         pl.ksplit = 1;
         pl.kb_per_split = (k * eb + kKBytes - 1) / kKBytes;
@@ -253,6 +254,7 @@ int launch_gemm_tc(int kind, const void* w, long long ldw_bytes, const void* a, 
     p.ws = pl.ksplit > 1 ? ws->ws : nullptr;
     p.counters = pl.ksplit > 1 ? ws->counters : nullptr;
     p.err = err;
+    p.store_guard = outs.store_guard ? 1 : 0;
     if (fq) {
         const long long k16 = (k + 15) & ~15;
         if (kind != 0 || outs.copies > 1 || !fq->a || !fq->a8 || !fq->scales || !fq->sync || fq->ld8 % 16 ||

@@ -48,6 +48,7 @@ struct GemmParams {
     int32_t* ws;         // split-K partial sums [m][n], all zero between launches
     unsigned* counters;  // split-K arrivals per tile, all zero between launches
     int* err;
+    int store_guard;  // OutMembers::store_guard
     // kFused
     const float* q_a;
     long long q_lda;
@@ -468,6 +469,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         const int half = e >> 2;  // 0 or 1
         const int etid = threadIdx.x - 96;
         bool waited_dep = false;
+        bool live = true;  // false: the call was rejected, store nothing
         if constexpr (MODE == kFused) {
             griddep_wait();  // the f32 activations come from the preceding work
             waited_dep = true;
@@ -484,11 +486,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
             if (!waited_dep) {
                 griddep_wait();
                 waited_dep = true;
+                if (p.store_guard) live = *reinterpret_cast<volatile const int*>(p.err) == 0;
             }
             // accumulator and output column this thread handles
             const int acc = C::kAcc == 2 ? half : 0;
             const int col = t.n0 + acc * 128 + q * 32 + lane;
-            const bool col_ok = col < p.n;
+            const bool col_ok = live && col < p.n;
             const int mi = member_of(p, col);
             float* out = p.out[mi];
             const long long ldo = p.ldo[mi];

@@ -29,6 +29,10 @@ struct OutMembers {
     long long ldo[4] = {0, 0, 0, 0};
     int copies = 1;
     float* copy_out[kMaxCopies] = {};
+    // no output store once *err != 0 at the start of the epilogue (after the
+    // preceding quantiser has finished): outputs in the caller's own host
+    // memory stay untouched when a call is rejected
+    bool store_guard = false;
 };
 
 // K1: Q4_K/Q5_K/Q6_K rows -> int8 rows [n, k] + per-row scales [n].
