@@ -303,7 +303,7 @@ int finish(Ctx* c) {
 
 // Context split-K workspace sized for a W8A8 GEMM of this shape.
 int context_ws(Ctx* c, size_t m, size_t n, size_t k, rk::GemmWorkspace* out) {
-    const rk::GemmPlan pl = rk::plan_gemm(0, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k));
+    const rk::GemmPlan pl = rk::plan_gemm(0, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), false);
     const size_t bytes = gemm_ws_bytes(pl);
     *out = rk::GemmWorkspace{};
     if (bytes == 0) return kOk;
@@ -1355,7 +1355,7 @@ int rocknpu_b200_quantize_rows(const float* a, size_t m, size_t k, int8_t* a_i8,
 
 size_t rocknpu_b200_gemm_workspace_bytes(size_t m, size_t n, size_t k) {
     if (m == 0 || n == 0 || k == 0 || m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff) return 0;
-    return gemm_ws_bytes(rk::plan_gemm(0, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k)));
+    return gemm_ws_bytes(rk::plan_gemm(0, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), false));
 }
 
 int rocknpu_b200_gemm_w8a8(const int8_t* a_i8, size_t ld_a, const float* a_scales, const int8_t* w_i8, size_t ld_w,
@@ -1369,8 +1369,9 @@ int rocknpu_b200_gemm_w8a8(const int8_t* a_i8, size_t ld_a, const float* a_scale
     om.n_start[1] = static_cast<int>(n);
     om.out[0] = out;
     om.ldo[0] = static_cast<long long>(ldo);
-    const rk::GemmWorkspace gws = gemm_ws_view(
-        workspace, workspace_bytes, rk::plan_gemm(0, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k)));
+    const rk::GemmWorkspace gws =
+        gemm_ws_view(workspace, workspace_bytes,
+                     rk::plan_gemm(0, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), false));
     const int e = rk::launch_gemm_tc(0, w_i8, static_cast<long long>(ld_w), a_i8, static_cast<long long>(ld_a),
                                      static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), w_scales, a_scales,
                                      om, acc_out, static_cast<long long>(n), status, static_cast<cudaStream_t>(stream),

@@ -123,7 +123,13 @@ int k_atoms(int wt, int bt) { return (wt == 128 && bt <= 128) ? 2 : 1; }
 // stages; the estimate is the larger of that and the HBM time of the unique
 // bytes.  Ties prefer more units (more SMs streaming), then the earlier
 // option.  K is split only for long-K shapes that would leave most SMs idle.
-GemmPlan plan_gemm(int kind, int m, int n, int k) {
+// Two-SM pair tiles (256 x bt over two CTAs, gemm_pair.cu) are taken for
+// long-K shapes with at least one full wave of pair units, where they
+// measured faster on B200 (cfg5 n=28672 k=8192: +8 % at m=1024, +5 % at
+// m=16384); on the prefill shapes (k <= 2048, or a partial wave of pairs)
+// the one-SM tiles measured faster, against what the per-SM byte count
+// alone predicts.
+GemmPlan plan_gemm(int kind, int m, int n, int k, bool allow_pair) {
     GemmPlan pl;
     const int eb = kind == 0 ? 1 : 2;
     const int num_kb = (k * eb + kKBytes - 1) / kKBytes;
@@ -152,8 +158,37 @@ GemmPlan plan_gemm(int kind, int m, int n, int k) {
             pl.bt = o.bt;
         }
     }
+    // two-SM pairs
+    const char* pair_env = std::getenv("ROCKNPU_B200_GEMM_PAIR");
+    const bool pair_off = pair_env != nullptr && pair_env[0] == '0';
+    const bool pair_force = pair_env != nullptr && pair_env[0] == '1';
+    const bool tile_forced =
+        std::getenv("ROCKNPU_B200_GEMM_WT") != nullptr || std::getenv("ROCKNPU_B200_GEMM_BT") != nullptr;
+    if (allow_pair && !pair_off && (pair_force || !tile_forced)) {
+        const int bt = m >= 256 ? 256 : 128;
+        const int units = ((n + 255) / 256) * ((m + bt - 1) / bt);
+        if (pair_force || (num_kb >= 32 && m >= 256 && units >= gemm_detail::pair_capacity(kind, bt))) {
+            pl.wt = 256;
+            pl.bt = bt;
+            pl.pair = true;
+        }
+        if (pair_force) {
+            if (const char* v = std::getenv("ROCKNPU_B200_GEMM_BT")) {
+                const int b = std::atoi(v);
+                if (b == 128 || b == 256) pl.bt = b;
+            }
+        }
+    }
+    if (pl.pair) {
+        pl.ksplit = 1;
+        pl.kb_per_split = num_kb;
+        pl.tiles = ((n + 255) / 256) * ((m + pl.bt - 1) / pl.bt);
+        return pl;
+    }
     // tuning overrides, result bit-identical: ROCKNPU_B200_GEMM_WT (128/256),
-    // ROCKNPU_B200_GEMM_BT (16..256), ROCKNPU_B200_GEMM_KSPLIT (>= 1)
+    // ROCKNPU_B200_GEMM_BT (16..256), ROCKNPU_B200_GEMM_KSPLIT (>= 1),
+    // ROCKNPU_B200_GEMM_PAIR (0: never two-SM tiles, 1: always, bt from
+    // ROCKNPU_B200_GEMM_BT when 128 or 256)
     if (const char* v = std::getenv("ROCKNPU_B200_GEMM_WT")) {
         const int w = std::atoi(v);
         if (w == 128 || w == 256) pl.wt = w;
@@ -188,7 +223,7 @@ GemmPlan plan_gemm(int kind, int m, int n, int k) {
 }
 
 size_t fused_quant_sync_elems(int m, int n, int k) {
-    const GemmPlan pl = plan_gemm(0, m, n, k);
+    const GemmPlan pl = plan_gemm(0, m, n, k, false);  // fused launches run one-SM tiles
     return static_cast<size_t>((m + pl.bt - 1) / pl.bt) + 1;
 }
 
@@ -216,7 +251,7 @@ int launch_gemm_tc(int kind, const void* w, long long ldw_bytes, const void* a, 
     const int eb = kind == 0 ? 1 : 2;
     if (outs.copies < 1 || outs.copies > kMaxCopies || (outs.copies > 1 && outs.count != 1))
         return cudaErrorInvalidValue;
-    GemmPlan pl = plan_gemm(kind, m, n, k);
+    GemmPlan pl = plan_gemm(kind, m, n, k, fq == nullptr && outs.copies == 1);
     if (pl.ksplit > 1 && (outs.copies > 1 || outs.store_guard || ws == nullptr || ws->ws == nullptr ||
                           ws->counters == nullptr || ws->ws_elems < pl.ws_elems ||
                           ws->counter_elems < pl.counter_elems)) {
@@ -270,6 +305,12 @@ int launch_gemm_tc(int kind, const void* w, long long ldw_bytes, const void* a, 
         p.q_scale = fq->scales;
         p.q_ready = fq->sync;
         p.q_exit = fq->sync + p.tiles_m;
+    }
+    if (pl.pair) {
+        // each CTA of a pair loads 128 weight rows and bt/2 token rows
+        if (!make_map(&p.tmap_w, w, eb, k, n, ldw_bytes, 128)) return cudaErrorInvalidValue;
+        if (!make_map(&p.tmap_a, a, eb, k, m, lda_bytes, pl.bt / 2)) return cudaErrorInvalidValue;
+        return gemm_detail::launch_pair(kind, pl, p, s);
     }
     if (!make_map(&p.tmap_w, w, eb, k, n, ldw_bytes, pl.wt)) return cudaErrorInvalidValue;
     if (!make_map(&p.tmap_a, a, eb, k, m, lda_bytes, pl.bt)) return cudaErrorInvalidValue;

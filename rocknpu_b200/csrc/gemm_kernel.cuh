@@ -650,10 +650,14 @@ int launch_kind(const GemmPlan& pl, GemmParams& p, cudaStream_t s) {
     }
 }
 
-// One per translation unit (gemm_plain.cu, gemm_fused.cu, gemm_gather.cu).
+// One per translation unit (gemm_plain.cu, gemm_fused.cu, gemm_gather.cu,
+// gemm_pair.cu).
 int launch_plain(int kind, const GemmPlan& pl, GemmParams& p, cudaStream_t s);
 int launch_fused(const GemmPlan& pl, GemmParams& p, cudaStream_t s);
 int launch_gather(const GemmPlan& pl, GemmParams& p, cudaStream_t s);
+int launch_pair(int kind, const GemmPlan& pl, GemmParams& p, cudaStream_t s);
+// Two-SM pairs of the 256 x bt configuration resident at once.
+int pair_capacity(int kind, int bt);
 
 }  // namespace gemm_detail
 }  // namespace rk

@@ -82,9 +82,11 @@ bool fused_quant_enabled(int m, int k);
 // splits and the workspace a split launch needs.
 struct GemmPlan {
     int wt = 128, bt = 128, ksplit = 1, kb_per_split = 1, tiles = 1;
+    bool pair = false;  // two-SM (cta_group::2) 256 x bt tiles, gemm_pair.cu
     size_t ws_elems = 0, counter_elems = 0;
 };
-GemmPlan plan_gemm(int kind, int m, int n, int k);
+// allow_pair: the launch may use the two-SM kernel (plain outputs only).
+GemmPlan plan_gemm(int kind, int m, int n, int k, bool allow_pair = true);
 
 // K3/K4: out = epilogue(W[n,k] . A[m,k]^T) on tcgen05.  kind 0: int8 inputs,
 // int32 accumulators, out = (f32(acc) * a_scale[m]) * w_scale[n]; kind 1:

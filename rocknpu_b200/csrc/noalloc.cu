@@ -89,7 +89,7 @@ extern "C" int rocknpu_b200_matmul_w8a8_noalloc(const float* a, const int8_t* w_
     // must start at zero and a previous call may have stopped mid-way, so it
     // is cleared here.
     rk::GemmWorkspace gws;
-    const rk::GemmPlan pl = rk::plan_gemm(0, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k));
+    const rk::GemmPlan pl = rk::plan_gemm(0, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), false);
     if (pl.ksplit > 1) {
         const size_t ws_off = needed;
         const size_t cbytes = align256(pl.counter_elems * sizeof(unsigned));

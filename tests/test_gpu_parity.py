@@ -173,6 +173,77 @@ def test_gemm_every_tile_configuration_exact(dev, rng, monkeypatch, wt, bt, m, k
     assert np.array_equal(_bits(out.cpu().numpy()), _bits(exp))
 
 
+PAIR_SHAPES = [(300, 1024, 640), (512, 2048, 2560), (257, 384, 300), (1000, 640, 1024), (64, 2048, 256),
+               (33, 256, 2304), (2048, 512, 4096), (200, 112, 1000)]
+
+
+@pytest.mark.parametrize("bt", [128, 256])
+@pytest.mark.parametrize("m,k,n", PAIR_SHAPES)
+def test_gemm_pair_tiles_exact(dev, rng, monkeypatch, bt, m, k, n):
+    """Two-SM (cta_group::2) 256 x bt tiles, forced: the same bits as the
+    oracle with ragged M, N and K edges, token halves that fall past M, and
+    several units per pair (accumulator buffers reused across units and
+    launches)."""
+    monkeypatch.setenv("ROCKNPU_B200_GEMM_PAIR", "1")
+    monkeypatch.setenv("ROCKNPU_B200_GEMM_BT", str(bt))
+    a8 = rng.integers(-127, 128, size=(m, k), dtype=np.int8)
+    w8 = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
+    a_s = rng.uniform(0.001, 0.1, size=m).astype(np.float32)
+    w_s = rng.uniform(0.001, 0.1, size=n).astype(np.float32)
+    acc_ref = oracle.gemm_i8_i32(a8, w8)
+    status = dev.new_status()
+    ta8, tas, tw8, tws = (torch.from_numpy(x).cuda() for x in (a8, a_s, w8, w_s))
+    for _ in range(2):
+        acc = torch.full((m, n), -7, dtype=torch.int32, device="cuda")
+        out = dev.gemm_w8a8(ta8, tas, tw8, tws, status, acc=acc)
+        torch.cuda.synchronize()
+        assert status.item() == 0
+        assert np.array_equal(acc.cpu().numpy(), acc_ref)
+    exp = np.empty((m, n), dtype=np.float32)
+    for r in range(m):
+        oracle.lib().orc_rescale_i32_row(oracle._p(np.ascontiguousarray(acc_ref[r])), oracle._p(w_s),
+                                         float(a_s[r]), oracle._p(exp[r]), n)
+    assert np.array_equal(_bits(out.cpu().numpy()), _bits(exp))
+
+
+@pytest.mark.parametrize("bt", [128, 256])
+@pytest.mark.parametrize("m,k,n", [(300, 1024, 640), (1000, 2048, 1536), (77, 512, 300)])
+def test_gemm_f16_pair_tiles(dev, rng, monkeypatch, bt, m, k, n):
+    a = rng.standard_normal((m, k)).astype(np.float16)
+    w = (rng.standard_normal((n, k)) * 0.05).astype(np.float16)
+    ta, tw = torch.from_numpy(a).cuda(), torch.from_numpy(w).cuda()
+    status = dev.new_status()
+    monkeypatch.setenv("ROCKNPU_B200_GEMM_PAIR", "0")
+    one_sm = dev.gemm_f16(ta, tw, status)
+    monkeypatch.setenv("ROCKNPU_B200_GEMM_PAIR", "1")
+    monkeypatch.setenv("ROCKNPU_B200_GEMM_BT", str(bt))
+    pair = dev.gemm_f16(ta, tw, status)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    ref = oracle.matmul_f16(w.view(np.uint16), a.astype(np.float32))
+    got = pair.cpu().numpy()
+    np.testing.assert_allclose(got, ref, rtol=1e-3, atol=1e-3 * np.abs(ref).max())
+    # the same f32 tensor-core accumulation as the one-SM tiles
+    assert np.array_equal(_bits(got), _bits(one_sm.cpu().numpy()))
+
+
+def test_pair_tiles_concat_group(ctx, rng, monkeypatch):
+    monkeypatch.setenv("ROCKNPU_B200_GEMM_PAIR", "1")
+    m, k = 320, 2048
+    ns, kinds = [2048, 256, 256], [4, 4, 6]
+    ws = [rk.synth_q_weights(kd, n, k, seed=80 + i) for i, (kd, n) in enumerate(zip(kinds, ns))]
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    outs = [np.full((m, n), np.nan, dtype=np.float32) for n in ns]
+    c = rk.Context()  # its own weight cache
+    try:
+        assert c.matmul_q_concat(ws, kinds, ns, a, outs, m, k) == 0
+    finally:
+        c.close()
+    for w, kd, n, o in zip(ws, kinds, ns, outs):
+        st, ref = oracle.matmul_q(kd, w, a, n)
+        assert np.array_equal(_bits(o), _bits(ref))
+
+
 @pytest.mark.parametrize("m", [4, 8, 12, 16, 32, 48, 64, 128])
 def test_gemm_mtile_kat(dev, m):
     # crates/rocket-smoke/src/bin/int8_mtile.rs:28-86
