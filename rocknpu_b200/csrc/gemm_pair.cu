@@ -14,9 +14,9 @@
 //
 // Barriers: full[s] lives in the even CTA and receives both CTAs' copy bytes
 // (the loads name it through the cluster window); empty[s] and tfull[b] are
-// signalled in both CTAs by the leader's multicast commit; tempty[b] in the
-// even CTA counts the epilogue warps of both CTAs.  No load is multicast:
-// every CTA reads its own half from global memory.  Every wait is bounded
+// signalled in both CTAs by one tcgen05.commit with a two-CTA mask; tempty[b]
+// in the even CTA counts the epilogue warps of both CTAs.  Every CTA reads
+// only its own operand halves from global memory.  Every wait is bounded
 // (kWaitLimitNs) and every path reaches the final cluster barrier, so both
 // CTAs of a pair leave together.
 #include "gemm_kernel.cuh"

@@ -223,7 +223,7 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
 
 // 2-D TMA tile load into this CTA's shared memory whose completion bytes
 // count on the barrier at shared::cluster address `bar_cluster` (the pair
-// leader's).  No multicast: each CTA loads its own half.
+// leader's).  Each CTA loads only its own half.
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int32_t x,
                                                  int32_t y) {
     asm volatile(
