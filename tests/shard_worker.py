@@ -76,8 +76,10 @@ def gpu_main(route: str) -> int:
     rank, world = dist.get_rank(), dist.get_world_size()
     failures = 0
     try:
+        # the last shape is long-K enough that each rank's GEMM runs two-SM
+        # pair tiles at two ranks (one-SM tiles at more)
         for kind, n, k, m in [(4, 2048, 2048, 128), (6, 1184, 512, 77), (4, 5632, 2048, 512), (4, 96, 256, 3),
-                              (4, 2048, 2048, 1)]:
+                              (4, 2048, 2048, 1), (4, 8192, 4096, 2048)]:
             blocks = rk.synth_q_weights(kind, n, k, seed=n + k, sigma=0.02)
             x = torch.from_numpy(rk.synth_normal(7 + m, m * k).reshape(m, k)).cuda()
             sm = shard.ShardedMatmul(kind, blocks, k, n, route=route, max_m=m)
