@@ -103,3 +103,54 @@ def test_tinyllama_pp512_layer_calls_through_the_c_abi(ctx):
     st, ref = oracle.matmul_q(kd, w, a2, n2)
     assert st == 0
     assert np.array_equal(out.view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("kind", [4, 6])
+def test_largest_plugin_shape_through_the_c_abi(ctx, kind):
+    """The largest MUL_MAT the plugin offloads on the prompt path
+    (ggml-rocknpu.cpp:614-715: k % 256 == 0 with ceil512(k) <= 12288, n % 32 == 0
+    with n <= 24576): k = 12288, n = 24576 -- the reference splits such a call
+    into <= 8192-column chunks (split_wide_mtile, capi/src/lib.rs:2136-2160),
+    which leaves every element's value unchanged -- at m = 320, bit for bit
+    against the oracle."""
+    m, k, n = 320, 12288, 24576
+    w = rk.synth_q_weights(kind, n, k, seed=70 + kind)
+    a = rk.synth_normal(71, m * k).reshape(m, k)
+    out = np.full((m, n), np.nan, dtype=np.float32)
+    assert rk.mul_mat_supported(rk.capi.GGML_Q4_K if kind == 4 else rk.capi.GGML_Q6_K, k, n, m)
+    assert ctx.matmul_q(kind, w, a, out, m, k, n) == 0
+    st, ref = oracle.matmul_q(kind, w, a, n)
+    assert st == 0
+    assert np.array_equal(out.view(np.uint32), ref.view(np.uint32))
+
+
+def test_tinyllama_pp512_whole_step_through_the_c_abi():
+    """Every MUL_MAT call of the default bench step (22 layers x {QKV group,
+    O, gate/up group, down} of the TinyLlama-shaped Q4_K_M prefill at 512
+    tokens, built by bench.py's own workload constructors) through the
+    reference C ABI, each member's output bit for bit against the oracle."""
+    import os
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+    bench.set_model("tinyllama")
+    m = 512
+    weights = bench.make_weights()
+    acts = bench.make_activations(m, seed=5000)
+    c = rk.Context()
+    try:
+        for key, blocks in weights.items():
+            _, members, k = bench.layer_plan(key[0])[["qkv", "o", "gate_up", "down"].index(key[1])]
+            a = acts[key]
+            outs = [np.full((m, n), np.nan, dtype=np.float32) for _, n in members]
+            if len(members) > 1:
+                st = c.matmul_q_concat(blocks, [kd for kd, _ in members], [n for _, n in members], a, outs, m, k)
+            else:
+                st = c.matmul_q(members[0][0], blocks[0], a, outs[0], m, k, members[0][1])
+            assert st == 0, key
+            for (kd, n), b, o in zip(members, blocks, outs):
+                st, ref = oracle.matmul_q(kd, b, a, n)
+                assert st == 0
+                assert np.array_equal(o.view(np.uint32), ref.view(np.uint32)), (key, kd, n)
+    finally:
+        c.close()
