@@ -70,7 +70,9 @@ struct Cfg {
     static constexpr int kStage = kWBytes + kABytes;
     static constexpr int kBarOffset = STAGES * kStage;
     static constexpr int kNumBars = 2 * STAGES + 5;
-    static constexpr int kBytes = kBarOffset + kNumBars * 8 + 32 + 1024;  // + alignment slack
+    // per epilogue warp, the token scales of its current unit
+    static constexpr int kScaleOffset = kBarOffset + kNumBars * 8 + 32;
+    static constexpr int kBytes = kScaleOffset + kEpiWarps * BT * 4 + 1024;  // + alignment slack
     // accumulator buffers: two (the epilogue of one unit overlaps the next
     // unit's MMAs) when they fit TMEM's 512 columns, else one (256 x 256)
     static constexpr int kBufs = 2 * kAcc * BT <= 512 ? 2 : 1;
@@ -475,16 +477,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
             waited_dep = true;
             fused_quant<BT>(p, sh, e, lane);
         }
+        float* tok_scale = reinterpret_cast<float*>(smem + C::kScaleOffset) + e * BT;
         int j = 0;
         for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++j) {
             const Unit t = unit_coords<WT, BT>(p, u);
             const int buf = j % C::kBufs, use = j / C::kBufs;
-            int ready = 0;
-            if (lane == 0) ready = wait_or_abort(&sh.tfull[buf], use & 1, sh.abort) ? 1 : 0;
-            ready = __shfl_sync(0xffffffffu, ready, 0);
-            if (!ready && lane == 0 && !*sh.abort) fail(p, sh, kErrTimeoutAccum);
+            const bool split = KIND == 0 && MODE != kGather && p.ksplit > 1;
             if (!waited_dep) {
-                griddep_wait();
+                griddep_wait();  // the token scales come from the preceding work
                 waited_dep = true;
                 if (p.store_guard) live = *reinterpret_cast<volatile const int*>(p.err) == 0;
             }
@@ -496,14 +496,27 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
             float* out = p.out[mi];
             const long long ldo = p.ldo[mi];
             const int ocol = col - p.n_start[mi];
+            // this unit's scales, loaded while its MMAs still run
             float wsc = 0.0f;
-            if constexpr (KIND == 0) wsc = col_ok ? p.w_scale[col] : 0.0f;
+            if constexpr (KIND == 0) wsc = col_ok ? __ldg(p.w_scale + col) : 0.0f;
+            if constexpr (KIND == 0 && MODE != kFused) {
+                if (!split) {
+                    for (int i = lane; i < BT; i += 32) {
+                        const int m = t.m0 + i;
+                        tok_scale[i] = m < p.m ? __ldg(p.a_scale + m) : 0.0f;
+                    }
+                    __syncwarp();
+                }
+            }
+            int ready = 0;
+            if (lane == 0) ready = wait_or_abort(&sh.tfull[buf], use & 1, sh.abort) ? 1 : 0;
+            ready = __shfl_sync(0xffffffffu, ready, 0);
+            if (!ready && lane == 0 && !*sh.abort) fail(p, sh, kErrTimeoutAccum);
             const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                                        static_cast<uint32_t>((buf * C::kAcc + acc) * BT);
             // with one accumulator the two halves split the token columns
             const int c_first = C::kAcc == 2 ? 0 : half * 16;
             const int c_step = C::kAcc == 2 ? 16 : 32;
-            const bool split = KIND == 0 && MODE != kGather && p.ksplit > 1;
             if constexpr (MODE == kFused) {
                 // token scales written by other CTAs' quantiser warps
                 if (ready && lane == 0) (void)ld_acquire_gpu(p.q_ready + t.m0 / BT);
@@ -519,12 +532,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                     // the chunk's token scales, loaded before any store of
                     // the chunk (stores could otherwise order every load)
                     float asv[16];
-                    if constexpr (KIND == 0) {
+                    if constexpr (KIND == 0 && MODE == kFused) {
 #pragma unroll
                         for (int jj = 0; jj < 16; ++jj) {
                             const int m = t.m0 + c + jj;
                             asv[jj] = (!split && m < p.m) ? load_scale<MODE>(a_scale + m) : 0.0f;
                         }
+                    } else if constexpr (KIND == 0) {
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj) asv[jj] = split ? 0.0f : tok_scale[c + jj];
                     }
                     uint32_t r[16];
                     tmem_ld16(lane_base + c, r);

@@ -32,7 +32,9 @@ struct PairCfg {
     static constexpr int kStages = (192 * 1024) / kStage;
     static constexpr int kBarOffset = kStages * kStage;
     static constexpr int kNumBars = 2 * kStages + 5;
-    static constexpr int kBytes = kBarOffset + kNumBars * 8 + 32 + 1024;  // + alignment slack
+    // per epilogue warp, the token scales of its current unit
+    static constexpr int kScaleOffset = kBarOffset + kNumBars * 8 + 32;
+    static constexpr int kBytes = kScaleOffset + kEpiWarps * BT * 4 + 1024;  // + alignment slack
     static constexpr uint32_t kTmemCols = 2 * BT;                         // two accumulator buffers
     static_assert(BT == 128 || BT == 256, "pair token tile");
     static_assert(kBytes <= 232448, "shared memory");
@@ -188,16 +190,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         bool live = true;
         const uint32_t tempty_leader0 = map_cluster(smem_u32(&tempty[0]), 0);
         const uint32_t tempty_leader1 = map_cluster(smem_u32(&tempty[1]), 0);
+        float* tok_scale = reinterpret_cast<float*>(smem + C::kScaleOffset) + e * BT;
         int j = 0;
         for (int u = pair; u < p.units; u += npairs, ++j) {
             const Unit t = unit_coords<256, BT>(p, u);
             const int buf = j & 1, use = j >> 1;
-            int ready = 0;
-            if (lane == 0) ready = wait_or_abort(&tfull[buf], use & 1, abort) ? 1 : 0;
-            ready = __shfl_sync(0xffffffffu, ready, 0);
-            if (!ready && lane == 0 && !*abort) fail(p, sh, kErrTimeoutAccum);
             if (!waited_dep) {
-                griddep_wait();
+                griddep_wait();  // the token scales come from the preceding work
                 waited_dep = true;
                 if (p.store_guard) live = *reinterpret_cast<volatile const int*>(p.err) == 0;
             }
@@ -207,23 +206,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             float* out = p.out[mi];
             const long long ldo = p.ldo[mi];
             const int ocol = col - p.n_start[mi];
+            // this unit's scales, loaded while its MMAs still run
             float wsc = 0.0f;
-            if constexpr (KIND == 0) wsc = col_ok ? p.w_scale[col] : 0.0f;
+            if constexpr (KIND == 0) {
+                wsc = col_ok ? __ldg(p.w_scale + col) : 0.0f;
+                for (int i = lane; i < BT; i += 32) {
+                    const int m = t.m0 + i;
+                    tok_scale[i] = m < p.m ? __ldg(p.a_scale + m) : 0.0f;
+                }
+                __syncwarp();
+            }
+            int ready = 0;
+            if (lane == 0) ready = wait_or_abort(&tfull[buf], use & 1, abort) ? 1 : 0;
+            ready = __shfl_sync(0xffffffffu, ready, 0);
+            if (!ready && lane == 0 && !*abort) fail(p, sh, kErrTimeoutAccum);
             const uint32_t lane_base =
                 tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BT);
             if (ready) {
                 tc_fence_after();
-                const float* __restrict__ a_scale = p.a_scale;
                 int32_t* __restrict__ acc_out = p.acc_out;
 #pragma unroll 1
                 for (int c = half * 16; c < BT; c += 32) {
                     float asv[16];
                     if constexpr (KIND == 0) {
 #pragma unroll
-                        for (int jj = 0; jj < 16; ++jj) {
-                            const int m = t.m0 + c + jj;
-                            asv[jj] = m < p.m ? __ldg(a_scale + m) : 0.0f;
-                        }
+                        for (int jj = 0; jj < 16; ++jj) asv[jj] = tok_scale[c + jj];
                     }
                     uint32_t r[16];
                     tmem_ld16(lane_base + c, r);

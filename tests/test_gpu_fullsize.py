@@ -75,8 +75,12 @@ def test_cfg5_gemm_int32_sampled_rows_and_linearity(cfg5_weight):
     assert np.array_equal(accs[0][rows].cpu().numpy(), ref)
 
 
-@pytest.fixture(scope="module")
+@pytest.fixture
 def ctx():
+    # one context per test: resident weights are cached by the host address
+    # of their bytes (the reference's DecodeWeightKey contract: weights stay
+    # alive and unchanged for the context's lifetime), and a test's freed
+    # arrays can hand their addresses to the next test's weights
     rk.apply_default_env()
     c = rk.Context()
     yield c

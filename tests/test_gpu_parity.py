@@ -26,8 +26,12 @@ def dev():
     return device
 
 
-@pytest.fixture(scope="module")
+@pytest.fixture
 def ctx():
+    # one context per test: resident weights are cached by the host address
+    # of their bytes (the reference's DecodeWeightKey contract: weights stay
+    # alive and unchanged for the context's lifetime), and a test's freed
+    # arrays can hand their addresses to the next test's weights
     rk.apply_default_env()
     c = rk.Context()
     yield c
