@@ -301,6 +301,61 @@ __global__ void __launch_bounds__(kRowThreads) quant_rows_kernel(const float* __
     if (threadIdx.x == 0) scales[row] = scale;
 }
 
+// K2 with the row in registers: 128 threads per row, NV float4 per thread
+// (k16 <= 512 NV), the same arithmetic as quant_rows_kernel (zero padding up
+// to k16 included).  It holds no row in shared memory and few registers, so
+// the GEMM that this kernel launches programmatically can become resident on
+// the SMs while the rows are quantised (its prologue and weight loads then
+// overlap this kernel).
+constexpr int kRegRowThreads = 128;
+
+template <int NV>
+__global__ void __launch_bounds__(kRegRowThreads) quant_rows_reg_kernel(const float* __restrict__ a, int k,
+                                                                         long long lda, int8_t* __restrict__ a8,
+                                                                         long long ld8, float* __restrict__ scales,
+                                                                         int* __restrict__ err) {
+    __shared__ float red[33];
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int row = blockIdx.x;
+    const float4* src = reinterpret_cast<const float4*>(a + static_cast<size_t>(row) * lda);
+    const int k4 = k >> 2, k16_4 = ((k + 15) & ~15) >> 2;
+    float4 v[NV];
+    float amax = 0.0f;
+    bool finite = true;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+        const int i = threadIdx.x + j * kRegRowThreads;
+        v[j] = i < k4 ? __ldg(src + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        finite &= isfinite(v[j].x) && isfinite(v[j].y) && isfinite(v[j].z) && isfinite(v[j].w);
+        amax = fmaxf(fmaxf(amax, fmaxf(fabsf(v[j].x), fabsf(v[j].y))), fmaxf(fabsf(v[j].z), fabsf(v[j].w)));
+    }
+    if (__syncthreads_or(!finite)) {
+        if (threadIdx.x == 0) atomicExch(err, kErrNonFinite);
+        return;
+    }
+    const float scale = row_scale(block_max(amax, red));
+    const float inv = row_inv(scale);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(a8 + static_cast<size_t>(row) * ld8);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+        const int i = threadIdx.x + j * kRegRowThreads;
+        if (i < k16_4) dst[i] = quant_pack4(v[j], scale, inv);
+    }
+    if (threadIdx.x == 0) scales[row] = scale;
+}
+
+template <int NV>
+bool launch_quant_reg(int nv, const float* a, int m, int k, long long lda, int8_t* a8, long long ld8, float* scales,
+                      int* err, cudaStream_t s) {
+    if constexpr (NV > 12) {
+        return false;
+    } else {
+        if (nv > NV) return launch_quant_reg<NV + (NV < 4 ? NV : 4)>(nv, a, m, k, lda, a8, ld8, scales, err, s);
+        quant_rows_reg_kernel<NV><<<m, kRegRowThreads, 0, s>>>(a, k, lda, a8, ld8, scales, err);
+        return true;
+    }
+}
+
 // HILO (hilo_stack, capi/src/lib.rs:2045-2070): residual rows of the
 // two-part activation encoding, res = x - f32(q) * scale with q, scale from
 // the row's own quantisation (two f32 roundings, as the reference).
@@ -426,7 +481,13 @@ void launch_dequant_f16(int kind, const uint8_t* blocks, int k, int n, __half* w
 
 void launch_quant_rows(const float* a, int m, int k, long long lda, int8_t* a8, long long ld8, float* scales,
                        int* err, cudaStream_t s) {
-    const size_t smem = static_cast<size_t>((k + 15) & ~15) * sizeof(float);
+    const int k16 = (k + 15) & ~15;
+    const int nv = (k16 / 4 + kRegRowThreads - 1) / kRegRowThreads;
+    if (k % 4 == 0 && lda % 4 == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0 && ld8 % 4 == 0 &&
+        (reinterpret_cast<uintptr_t>(a8) & 3) == 0 && k16 <= ld8 && nv <= 12 &&
+        launch_quant_reg<1>(nv, a, m, k, lda, a8, ld8, scales, err, s))
+        return;
+    const size_t smem = static_cast<size_t>(k16) * sizeof(float);
     set_smem(quant_rows_kernel, smem);
     quant_rows_kernel<<<m, kRowThreads, smem, s>>>(a, k, lda, a8, ld8, scales, err);
 }
