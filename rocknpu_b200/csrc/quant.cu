@@ -398,6 +398,9 @@ __global__ void add_halves_kernel(const float* __restrict__ hi, const float* __r
 // 16-byte (f32) / 8-byte (f16) aligned.
 __global__ void f32_to_f16_kernel(const float* __restrict__ a, int m, int k, long long lda, __half* __restrict__ out,
                                   long long ldo, bool vec) {
+    // the FP16 GEMM that follows may start its prologue and weight loads now
+    // (it reads these rows only after its griddepcontrol.wait)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     for (int r = blockIdx.x; r < m; r += gridDim.x) {
         const float* src = a + static_cast<long long>(r) * lda;
         __half* dst = out + static_cast<long long>(r) * ldo;
