@@ -235,7 +235,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     uint32_t r[16];
                     tmem_ld16(lane_base + c, r);
                     tmem_ld_wait();
-                    if (col_ok) {
+                    if (col_ok && acc_out == nullptr && t.m0 + c + 16 <= p.m) {
+                        // a whole chunk, no per-element branch
+                        float* __restrict__ o = out + static_cast<long long>(t.m0 + c) * ldo + ocol;
+                        float v[16];
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj) {
+                            if constexpr (KIND == 0)
+                                v[jj] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[jj])), asv[jj]), wsc);
+                            else
+                                v[jj] = __uint_as_float(r[jj]);
+                        }
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj) o[jj * ldo] = v[jj];
+                    } else if (col_ok) {
                         float* __restrict__ o = out + static_cast<long long>(t.m0 + c) * ldo + ocol;
 #pragma unroll
                         for (int jj = 0; jj < 16; ++jj) {

@@ -344,6 +344,23 @@ __global__ void __launch_bounds__(kRegRowThreads) quant_rows_reg_kernel(const fl
     if (threadIdx.x == 0) scales[row] = scale;
 }
 
+// SMs running this kernel keep the largest shared-memory partition, so a
+// GEMM CTA (~200 KB of shared memory) launched programmatically behind it can
+// become resident beside its CTAs; with the default carveout the SM must
+// drain and be reconfigured first.
+template <typename F>
+void prefer_max_shared(F* f) {
+    static bool done[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && done[dev]) return;
+    if (cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared) ==
+            cudaSuccess &&
+        dev >= 0 && dev < 64)
+        done[dev] = true;
+    cudaGetLastError();
+}
+
 template <int NV>
 bool launch_quant_reg(int nv, const float* a, int m, int k, long long lda, int8_t* a8, long long ld8, float* scales,
                       int* err, cudaStream_t s) {
@@ -351,6 +368,7 @@ bool launch_quant_reg(int nv, const float* a, int m, int k, long long lda, int8_
         return false;
     } else {
         if (nv > NV) return launch_quant_reg<NV + (NV < 4 ? NV : 4)>(nv, a, m, k, lda, a8, ld8, scales, err, s);
+        prefer_max_shared(quant_rows_reg_kernel<NV>);
         quant_rows_reg_kernel<NV><<<m, kRegRowThreads, 0, s>>>(a, k, lda, a8, ld8, scales, err);
         return true;
     }
@@ -499,6 +517,7 @@ void launch_f32_to_f16(const float* a, int m, int k, long long lda, __half* out,
     const bool vec = k % 4 == 0 && lda % 4 == 0 && ldo % 4 == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0 &&
                      (reinterpret_cast<uintptr_t>(out) & 7) == 0;
     const int blocks = std::max(1, std::min(m, 148 * 8));
+    prefer_max_shared(f32_to_f16_kernel);
     f32_to_f16_kernel<<<blocks, 256, 0, s>>>(a, m, k, lda, out, ldo, vec);
 }
 
