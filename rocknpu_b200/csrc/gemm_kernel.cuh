@@ -71,7 +71,7 @@ struct Cfg {
     static constexpr int kBarOffset = STAGES * kStage;
     static constexpr int kNumBars = 2 * STAGES + 5;
     // per epilogue warp, the token scales of its current unit
-    static constexpr int kScaleOffset = kBarOffset + kNumBars * 8 + 32;
+    static constexpr int kScaleOffset = (kBarOffset + kNumBars * 8 + 32 + 15) & ~15;  // 16-byte aligned
     static constexpr int kBytes = kScaleOffset + kEpiWarps * BT * 4 + 1024;  // + alignment slack
     // accumulator buffers: two (the epilogue of one unit overlaps the next
     // unit's MMAs) when they fit TMEM's 512 columns, else one (256 x 256)
@@ -539,8 +539,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                             asv[jj] = (!split && m < p.m) ? load_scale<MODE>(a_scale + m) : 0.0f;
                         }
                     } else if constexpr (KIND == 0) {
+                        // four 16-byte reads (tok_scale and c are 16-byte aligned)
 #pragma unroll
-                        for (int jj = 0; jj < 16; ++jj) asv[jj] = split ? 0.0f : tok_scale[c + jj];
+                        for (int jj = 0; jj < 16; jj += 4) {
+                            const float4 s4 = *reinterpret_cast<const float4*>(tok_scale + c + jj);
+                            asv[jj] = s4.x;
+                            asv[jj + 1] = s4.y;
+                            asv[jj + 2] = s4.z;
+                            asv[jj + 3] = s4.w;
+                        }
                     }
                     uint32_t r[16];
                     tmem_ld16(lane_base + c, r);

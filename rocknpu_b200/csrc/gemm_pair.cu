@@ -33,7 +33,7 @@ struct PairCfg {
     static constexpr int kBarOffset = kStages * kStage;
     static constexpr int kNumBars = 2 * kStages + 5;
     // per epilogue warp, the token scales of its current unit
-    static constexpr int kScaleOffset = kBarOffset + kNumBars * 8 + 32;
+    static constexpr int kScaleOffset = (kBarOffset + kNumBars * 8 + 32 + 15) & ~15;  // 16-byte aligned
     static constexpr int kBytes = kScaleOffset + kEpiWarps * BT * 4 + 1024;  // + alignment slack
     static constexpr uint32_t kTmemCols = 2 * BT;                         // two accumulator buffers
     static_assert(BT == 128 || BT == 256, "pair token tile");
@@ -229,8 +229,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 for (int c = half * 16; c < BT; c += 32) {
                     float asv[16];
                     if constexpr (KIND == 0) {
+                        // four 16-byte reads (tok_scale and c are 16-byte aligned)
 #pragma unroll
-                        for (int jj = 0; jj < 16; ++jj) asv[jj] = tok_scale[c + jj];
+                        for (int jj = 0; jj < 16; jj += 4) {
+                            const float4 s4 = *reinterpret_cast<const float4*>(tok_scale + c + jj);
+                            asv[jj] = s4.x;
+                            asv[jj + 1] = s4.y;
+                            asv[jj + 2] = s4.z;
+                            asv[jj + 3] = s4.w;
+                        }
                     }
                     uint32_t r[16];
                     tmem_ld16(lane_base + c, r);
