@@ -88,6 +88,30 @@ def test_device_entry_points_reject_bad_arguments():
     assert L.rocknpu_b200_gemm_workspace_bytes(0, 1, 1) == 0
 
 
+def test_host_buffer_entry_points_without_gpu():
+    """rocknpu_b200_host_alloc / _free / _host_mapped on a machine with no
+    GPU: nothing can be page-locked, so allocation returns NULL (and the
+    Python helper raises), freeing NULL is a no-op, freeing any other pointer
+    is rejected, and no host range counts as device-mapped."""
+    try:
+        import torch
+        if torch.cuda.is_available():
+            pytest.skip("a GPU is present")
+    except Exception:
+        pass
+    import numpy as np
+    L = rk.lib()
+    assert L.rocknpu_b200_host_alloc(1 << 20) is None
+    assert L.rocknpu_b200_host_alloc(0) is None
+    with pytest.raises(RuntimeError):
+        rk.host_empty((16, 16))
+    assert L.rocknpu_b200_host_free(None) == rk.STATUS_OK
+    a = np.zeros(1024, dtype=np.float32)
+    assert L.rocknpu_b200_host_free(a.ctypes.data) == rk.STATUS_INVALID_ARGUMENT
+    assert L.rocknpu_b200_host_mapped(a.ctypes.data, a.nbytes) == 0
+    assert L.rocknpu_b200_host_mapped(None, 16) == 0
+
+
 # ---- ggml plugin supports_op rules (ggml-rocknpu.cpp:614-715) ---------------
 
 ENV = ["ROCKNPU_W8_DIRECT_SUBMIT", "ROCKNPU_EXPERIMENT_DIRECT_SCRATCH", "ROCKNPU_PREFILL_CACHE",
