@@ -586,8 +586,9 @@ def cpu_baseline(weights, acts, m, budget_s=10.0):
     _, step_ops = algorithmic(m)
     step_s = dt * step_ops / ops_done
     return {"value": round(m / step_s, 2), "unit": "tok/s", "cores": oracle.threads(), "kind": "port",
-            "sample": f"{calls} MUL_MAT calls of layers 0-1 on {rows} of {m} tokens (quantize + int32 GEMM + "
-                      f"rescale, prepared weights), {dt:.1f} s, scaled by int8 ops to one {LAYERS}-layer step"}
+            "sample": f"{calls} MUL_MAT calls of layers 0-1 on {rows} of {m} tokens (quantize + int32 GEMM on "
+                      f"{oracle.gemm_path(rows, HIDDEN, HIDDEN)} + rescale, prepared weights), {dt:.1f} s, scaled by "
+                      f"int8 ops to one {LAYERS}-layer step"}
 
 
 def run_reference(args, rank: int, world: int):
@@ -632,7 +633,8 @@ def run_reference(args, rank: int, world: int):
                    "seq_len": m, "layers": LAYERS},
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": oracle.threads(), "kind": "port",
                          "sample": f"each step runs all {len(prepared)} MUL_MAT calls of the {LAYERS} layers on "
-                                   f"{m} tokens (quantize + int32 GEMM + rescale on prepared weights)"},
+                                   f"{m} tokens (quantize + int32 GEMM on {oracle.gemm_path(m, HIDDEN, HIDDEN)} + "
+                                   "rescale on prepared weights)"},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     return line

@@ -53,6 +53,8 @@ def lib():
         L.orc_quantize_symmetric_into.argtypes = [P, S, P, P]
         L.orc_prepare_w8a8.restype = ctypes.c_int
         L.orc_prepare_w8a8.argtypes = [ctypes.c_uint32, P, S, S, S, P, P]
+        L.orc_gemm_path.restype = ctypes.c_int
+        L.orc_gemm_path.argtypes = [S, S, S]
         L.orc_gemm_i8_i32.restype = None
         L.orc_gemm_i8_i32.argtypes = [P, P, P, S, S, S]
         L.orc_rescale_i32_row.restype = None
@@ -126,6 +128,11 @@ def prepare_w8a8(kind: int, blocks: np.ndarray, k: int, n: int):
     s = np.empty(n, dtype=np.float32)
     st = lib().orc_prepare_w8a8(kind, _p(blocks), blocks.size, k, n, _p(w), _p(s))
     return st, w, s
+
+
+def gemm_path(m: int, k: int, n: int) -> str:
+    """The CPU path of the exact int8 GEMM for this shape: amx, vnni or scalar."""
+    return {2: "amx", 1: "vnni", 0: "scalar"}[int(lib().orc_gemm_path(m, k, n))]
 
 
 def gemm_i8_i32(a: np.ndarray, w: np.ndarray) -> np.ndarray:

@@ -19,6 +19,20 @@
 #include <omp.h>
 #endif
 
+
+/* Grow-only per-thread scratch for the oracle's large temporaries: fresh
+ * multi-MB allocations fault in page by page on every call, which on some
+ * hosts costs more than the arithmetic being measured.  Each calling thread
+ * keeps its own buffers, so the oracle stays reentrant across threads. */
+static void *orc_scratch(void **slot, size_t *cap, size_t bytes) {
+    if (bytes > *cap) {
+        free(*slot);
+        *slot = malloc(bytes);
+        *cap = *slot ? bytes : 0;
+    }
+    return *slot;
+}
+
 #define QK_K 256
 
 int orc_threads(void) {
@@ -236,7 +250,10 @@ int orc_prepare_w8a8(uint32_t kind, const uint8_t *bytes, size_t nbytes, size_t 
  * like the K-split host accumulation (capi/src/lib.rs:1906-1914); for
  * |x| <= 127 and K <= 2^17 no wrap occurs. */
 #if defined(__x86_64__)
+#include <cpuid.h>
 #include <immintrin.h>
+#include <sys/syscall.h>
+#include <unistd.h>
 
 /* The same exact product with AVX-512 VNNI (the CPU baseline's fast path):
  * vpdpbusd multiplies unsigned by signed bytes, so A is offset to a + 128
@@ -293,11 +310,151 @@ static void gemm_vnni(const int8_t *a, const int8_t *w, int32_t *c, size_t m, si
 }
 #endif
 
-void orc_gemm_i8_i32(const int8_t *a, const int8_t *w, int32_t *c, size_t m, size_t k, size_t n) {
+/* The same exact product on AMX tiles (tdpbssd: signed x signed bytes, four
+ * per int32 lane, exact int32 accumulation).  A is copied zero-padded to
+ * 32-row / 64-byte blocks; W is packed once per call into the tile layout of
+ * the B operand (row r of a 16-column, 64-byte-deep block holds, for each of
+ * the 16 columns, its 4 bytes at depth 4r..4r+3).  Each thread computes 32 x 32
+ * blocks of C in four accumulator tiles. */
+#define ORC_ARCH_REQ_XCOMP_PERM 0x1023
+#define ORC_XFEATURE_XTILEDATA 18
+
+static int amx_ready(void) {
+    static int state = -1;
+    if (state >= 0) return state;
+    unsigned eax = 0, ebx = 0, ecx = 0, edx = 0;
+    state = 0;
+    if (!__get_cpuid_count(7, 0, &eax, &ebx, &ecx, &edx)) return state;
+    if (!((edx >> 24) & 1) || !((edx >> 25) & 1)) return state; /* AMX-TILE, AMX-INT8 */
+    if (syscall(SYS_arch_prctl, ORC_ARCH_REQ_XCOMP_PERM, ORC_XFEATURE_XTILEDATA) != 0) return state;
+    state = 1;
+    return state;
+}
+
+struct orc_tilecfg {
+    uint8_t palette_id;
+    uint8_t start_row;
+    uint8_t reserved[14];
+    uint16_t colsb[16];
+    uint8_t rows[16];
+};
+
+__attribute__((target("amx-tile,amx-int8")))
+static void gemm_amx(const int8_t *a, const int8_t *w, int32_t *c, size_t m, size_t k, size_t n) {
+    const size_t kp = (k + 63) / 64 * 64, mp = (m + 31) / 32 * 32, np = (n + 31) / 32 * 32;
+    const size_t kb = kp / 64;
+    static __thread void *ap_buf, *wp_buf;
+    static __thread size_t ap_cap, wp_cap;
+    int8_t *ap = (int8_t *)orc_scratch(&ap_buf, &ap_cap, mp * kp);
+    int8_t *wp = (int8_t *)orc_scratch(&wp_buf, &wp_cap, np * kp);
+    if (!ap || !wp) abort();
+    /* zero padding: A's rows past m and columns past k, W's packed bytes past n or k */
+#pragma omp parallel for schedule(static)
+    for (long i = 0; i < (long)mp; ++i) {
+        if (i < (long)m) {
+            memcpy(ap + (size_t)i * kp, a + (size_t)i * k, k);
+            memset(ap + (size_t)i * kp + k, 0, kp - k);
+        } else {
+            memset(ap + (size_t)i * kp, 0, kp);
+        }
+    }
+    if (np != n || kp != k) memset(wp, 0, np * kp);
+    /* wp[(t * kb + b) * 1024 + r * 64 + q * 4 + e] = w[t*16 + q][b*64 + 4r + e] */
+#pragma omp parallel for schedule(static) collapse(2)
+    for (long t = 0; t < (long)(np / 16); ++t) {
+        for (long b = 0; b < (long)kb; ++b) {
+            int8_t *blk = wp + ((size_t)t * kb + (size_t)b) * 1024;
+            const size_t k0 = (size_t)b * 64;
+            for (int q = 0; q < 16; ++q) {
+                const size_t col = (size_t)t * 16 + q;
+                if (col >= n) continue;
+                const int8_t *src = w + col * k + k0;
+                if (k - k0 >= 64) {
+                    for (int r = 0; r < 16; ++r) memcpy(blk + r * 64 + q * 4, src + 4 * r, 4);
+                } else {
+                    for (size_t kk = 0; kk < k - k0; ++kk) blk[(kk / 4) * 64 + q * 4 + kk % 4] = src[kk];
+                }
+            }
+        }
+    }
+    struct orc_tilecfg cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.palette_id = 1;
+    for (int t = 0; t < 8; ++t) {
+        cfg.rows[t] = 16;
+        cfg.colsb[t] = 64;
+    }
+    const long mblocks = (long)(mp / 32), nblocks = (long)(np / 32);
+#pragma omp parallel
+    {
+        _tile_loadconfig(&cfg);
+        int32_t out[32 * 32];
+#pragma omp for schedule(dynamic, 2) collapse(2)
+        for (long mb = 0; mb < mblocks; ++mb) {
+            for (long nb = 0; nb < nblocks; ++nb) {
+                _tile_zero(0);
+                _tile_zero(1);
+                _tile_zero(2);
+                _tile_zero(3);
+                const int8_t *a0 = ap + (size_t)mb * 32 * kp;
+                const int8_t *b0 = wp + (size_t)(nb * 2) * kb * 1024;
+                const int8_t *b1 = wp + (size_t)(nb * 2 + 1) * kb * 1024;
+                for (size_t b = 0; b < kb; ++b) {
+                    _tile_loadd(4, a0 + b * 64, kp);
+                    _tile_loadd(5, a0 + 16 * kp + b * 64, kp);
+                    _tile_loadd(6, b0 + b * 1024, 64);
+                    _tile_loadd(7, b1 + b * 1024, 64);
+                    _tile_dpbssd(0, 4, 6);
+                    _tile_dpbssd(1, 4, 7);
+                    _tile_dpbssd(2, 5, 6);
+                    _tile_dpbssd(3, 5, 7);
+                }
+                _tile_stored(0, out, 128);
+                _tile_stored(1, out + 16, 128);
+                _tile_stored(2, out + 16 * 32, 128);
+                _tile_stored(3, out + 16 * 32 + 16, 128);
+                for (int i = 0; i < 32; ++i) {
+                    const size_t row = (size_t)mb * 32 + i;
+                    if (row >= m) break;
+                    const size_t col0 = (size_t)nb * 32;
+                    const size_t cols = n - col0 < 32 ? n - col0 : 32;
+                    memcpy(c + row * n + col0, out + i * 32, cols * sizeof(int32_t));
+                }
+            }
+        }
+        _tile_release();
+    }
+}
+
+/* Which path orc_gemm_i8_i32 takes for this shape: 2 AMX, 1 AVX-512 VNNI,
+ * 0 the plain loops. */
+int orc_gemm_path(size_t m, size_t k, size_t n) {
 #if defined(__x86_64__)
     const char *force = getenv("ORACLE_SCALAR_GEMM");
-    if ((!force || force[0] != '1') && k <= ((size_t)1 << 17) && __builtin_cpu_supports("avx512f") &&
-        __builtin_cpu_supports("avx512bw") && __builtin_cpu_supports("avx512vnni")) {
+    const char *path = getenv("ORACLE_GEMM_PATH");
+    const int scalar = (force && force[0] == '1') || (path && !strcmp(path, "scalar"));
+    const int want_vnni = path && !strcmp(path, "vnni");
+    const int want_amx = path && !strcmp(path, "amx");
+    if (!scalar && !want_vnni && k <= ((size_t)1 << 17) && (want_amx || (m >= 16 && n >= 16)) && amx_ready())
+        return 2;
+    if (!scalar && k <= ((size_t)1 << 17) && __builtin_cpu_supports("avx512f") &&
+        __builtin_cpu_supports("avx512bw") && __builtin_cpu_supports("avx512vnni"))
+        return 1;
+#endif
+    (void)m, (void)k, (void)n;
+    return 0;
+}
+
+/* ORACLE_GEMM_PATH = amx | vnni | scalar forces one path (all give the same
+ * exact int32 results); ORACLE_SCALAR_GEMM=1 is the same as "scalar". */
+void orc_gemm_i8_i32(const int8_t *a, const int8_t *w, int32_t *c, size_t m, size_t k, size_t n) {
+#if defined(__x86_64__)
+    const int path = orc_gemm_path(m, k, n);
+    if (path == 2) {
+        gemm_amx(a, w, c, m, k, n);
+        return;
+    }
+    if (path == 1) {
         gemm_vnni(a, w, c, m, k, n);
         return;
     }
@@ -345,9 +502,12 @@ int orc_quantize_rows(const float *a, size_t m, size_t k, int8_t *a_i8, float *a
  * execute_cached_w8a8_m1, capi/src/lib.rs:1567-1701). */
 int orc_matmul_w8a8(const int8_t *w, const float *w_scales, const float *a, float *out,
                     int32_t *acc_out, size_t m, size_t k, size_t n) {
-    int8_t *a8 = (int8_t *)malloc(m * k);
-    float *as = (float *)malloc(m * sizeof(float));
-    int32_t *acc = acc_out ? acc_out : (int32_t *)malloc(m * n * sizeof(int32_t));
+    static __thread void *a8_buf, *as_buf, *acc_buf;
+    static __thread size_t a8_cap, as_cap, acc_cap;
+    int8_t *a8 = (int8_t *)orc_scratch(&a8_buf, &a8_cap, m * k);
+    float *as = (float *)orc_scratch(&as_buf, &as_cap, m * sizeof(float));
+    int32_t *acc = acc_out ? acc_out : (int32_t *)orc_scratch(&acc_buf, &acc_cap, m * n * sizeof(int32_t));
+    if (!a8 || !as || !acc) abort();
     int status = orc_quantize_rows(a, m, k, a8, as);
     if (status == ORC_OK) {
         orc_gemm_i8_i32(a8, w, acc, m, k, n);
@@ -355,9 +515,6 @@ int orc_matmul_w8a8(const int8_t *w, const float *w_scales, const float *a, floa
         for (long r = 0; r < (long)m; ++r)
             orc_rescale_i32_row(acc + (size_t)r * n, w_scales, as[r], out + (size_t)r * n, n);
     }
-    if (!acc_out) free(acc);
-    free(a8);
-    free(as);
     return status;
 }
 

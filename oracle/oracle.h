@@ -48,6 +48,9 @@ int orc_quantize_symmetric_into(const float *values, size_t len, int8_t *out, fl
 int orc_prepare_w8a8(uint32_t kind, const uint8_t *bytes, size_t nbytes, size_t k, size_t n,
                      int8_t *w_out, float *scales_out);
 
+/* 2: AMX tiles, 1: AVX-512 VNNI, 0: plain loops (the path orc_gemm_i8_i32
+ * takes for this shape on this CPU). */
+int orc_gemm_path(size_t m, size_t k, size_t n);
 void orc_gemm_i8_i32(const int8_t *a, const int8_t *w, int32_t *c, size_t m, size_t k, size_t n);
 
 void orc_rescale_i32_row(const int32_t *values, const float *w_scales, float a_scale, float *out,

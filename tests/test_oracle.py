@@ -186,14 +186,19 @@ def test_hilo_stack_and_sum_restatement():
 
 
 @pytest.mark.parametrize("m,k,n", [(1, 1, 1), (5, 100, 7), (64, 2048, 256), (17, 8192, 33), (3, 65, 130)])
-def test_gemm_fast_path_equals_scalar_loops(monkeypatch, m, k, n):
-    """The CPU baseline's AVX-512 VNNI product (unsigned-offset trick) is the
-    same exact int32 result as the plain loops and as int64 arithmetic."""
+@pytest.mark.parametrize("path", ["amx", "vnni"])
+def test_gemm_fast_path_equals_scalar_loops(monkeypatch, path, m, k, n):
+    """The CPU baseline's fast products -- AMX tiles (tdpbssd) and AVX-512 VNNI
+    (vpdpbusd with the unsigned-offset trick), each where the CPU has it, else
+    the next path down -- are the same exact int32 result as the plain loops
+    and as int64 arithmetic."""
     rng = np.random.default_rng(m * 31 + k)
     a = rng.integers(-127, 128, size=(m, k), dtype=np.int8)
     w = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
+    monkeypatch.setenv("ORACLE_GEMM_PATH", path)
     fast = oracle.gemm_i8_i32(a, w)
-    monkeypatch.setenv("ORACLE_SCALAR_GEMM", "1")
+    monkeypatch.setenv("ORACLE_GEMM_PATH", "scalar")
+    assert oracle.gemm_path(m, k, n) == "scalar"
     slow = oracle.gemm_i8_i32(a, w)
     assert np.array_equal(fast, slow)
     assert np.array_equal(fast, (a.astype(np.int64) @ w.astype(np.int64).T).astype(np.int32))
