@@ -142,9 +142,8 @@ int rocknpu_b200_matmul_w8a8(rocknpu_context *context, const float *a, const int
 
 /* The same W8A8 MUL_MAT as rocknpu_b200_matmul_w8a8, for callers that may not
  * allocate GPU memory once they are running: a runtime whose memory plan is
- * fixed at start-up, code that runs while a stream is being captured into a
- * CUDA graph (cudaMalloc is not allowed there), or a framework whose own
- * allocator must own every byte.  This entry point has no counterpart in the
+ * fixed at start-up (a serving loop or an embedded deployment with a static
+ * budget), or a framework whose own allocator must own every byte.  This entry point has no counterpart in the
  * reference interface.  It needs no context and calls no cudaMalloc,
  * cudaFree or allocating library routine: the int8 activations, per-token
  * scales and split-K sums live in a 16 MiB array inside the library's device

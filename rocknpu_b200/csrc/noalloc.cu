@@ -4,9 +4,8 @@
 // split-K partial sums in buffers the context allocates on demand.  Some
 // callers cannot let a library call cudaMalloc: a runtime that fixes its
 // whole memory plan at start-up and forbids allocation afterwards (real-time
-// serving loops, embedded deployments with a static budget), code running
-// while a stream is being captured into a CUDA graph (where cudaMalloc is not
-// allowed), or a host framework whose own allocator must own every byte.
+// serving loops, embedded deployments with a static budget), or a host
+// framework whose own allocator must own every byte.
 // For them this file keeps that scratch in one fixed-size array in the
 // library's device memory, so the call only launches kernels.
 #include <cuda_runtime.h>

@@ -1,8 +1,8 @@
 """The allocation-free W8A8 entry point (rocknpu_b200_matmul_w8a8_noalloc).
 
-It serves callers that may not allocate GPU memory once running (fixed
-memory plans, stream capture, foreign allocators) by keeping its scratch in
-a fixed array inside the library.  The test calls it through the C ABI and
+It serves callers that may not allocate GPU memory once running (a memory
+plan fixed at start-up, or a framework allocator that must own every byte)
+by keeping its scratch in a fixed array inside the library.  The test calls it through the C ABI and
 checks it against the context entry point rocknpu_b200_matmul_w8a8 on two
 calls in a row, bit-exact (the tolerance every W8A8 test here uses), so that
 contents left in the shared scratch by the first call cannot leak into the
