@@ -754,10 +754,11 @@ def run_ours_f16(args, rank: int, world: int):
         h2d = sum(4 * m * k for (_, _, _, n, k) in calls)
         d2h = sum(4 * m * n for (_, _, _, n, k) in calls)
         e2e = {"value": round(m / e2e_s, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "ms_per_step": round(e2e_s * 1e3, 3), "path": "rocknpu_matmul_f16_f32_f32 per member, rocknpu_b200_host_alloc host buffers"}
+               "ms_per_step": round(e2e_s * 1e3, 3),
+               "path": "rocknpu_matmul_f16_f32_f32 per member, rocknpu_b200_host_alloc host buffers"}
         ctx.close()
     cpu = None
-    if not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rows = min(m, 128)
         t1 = time.perf_counter()
         done = 0
