@@ -22,8 +22,10 @@ weight cache), 1.0 GB per step > L2, so no extra L2 flush is needed.
   rocknpu_matmul_q{4,6}_k_f32_f32 for O and down): H2D of every activation
   and D2H of every output inside the timed region.
 * cpu_baseline / --impl reference: the reference's CPU path restated in C
-  (oracle/, OpenMP, all host threads): per-token quantisation, int32 GEMM,
-  rescale -- timed on a bounded sample of the same workload.
+  (oracle/, OpenMP, all host threads): per-token quantisation, exact int32
+  GEMM (AMX tiles where the CPU has them, else AVX-512 VNNI; the line's
+  "sample" names the path), rescale -- timed on a bounded sample of the same
+  workload.
 
 Other configs: --workload llama32-1b (configs[2], pp512) and qwen25-1.5b
 (configs[3], pp2048) replay those models' MUL_MAT calls the same way;
