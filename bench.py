@@ -269,9 +269,14 @@ class ClockSampler:
 # workload construction
 # ---------------------------------------------------------------------------
 
-def make_weights(seed: int = 1000):
-    """Host K-quant blocks per layer and call: {(layer, call): [blocks...]}."""
-    import rocknpu_b200 as rk
+def make_weights(seed: int = 1000, gen=None):
+    """Host K-quant blocks per layer and call: {(layer, call): [blocks...]}.
+    `gen` supplies synth_q_weights: the library (our arm) or the oracle's
+    byte-identical generator (the reference arm, whose process must not load
+    the library)."""
+    if gen is None:
+        import rocknpu_b200 as gen
+    rk = gen
     weights = {}
     s = seed
     for layer in range(LAYERS):
@@ -284,8 +289,10 @@ def make_weights(seed: int = 1000):
     return weights
 
 
-def make_activations(m: int, seed: int):
-    import rocknpu_b200 as rk
+def make_activations(m: int, seed: int, gen=None):
+    if gen is None:
+        import rocknpu_b200 as gen
+    rk = gen
     acts = {}
     s = seed
     for layer in range(LAYERS):
@@ -536,10 +543,7 @@ def run_ours(args, rank: int, world: int):
         "vs_baseline": None,
         "dtype": "int8 (W8A8, int32 accumulate, f32 out)",
         "data": "synthetic (random-init N(0,0.02^2) -> Q4_K/Q6_K weights, N(0,1) activations)",
-        "config": {"workload": workload_name(m), "tokens_per_step": m,
-                   "global_batch": world * m, "seq_len": m, "layers": LAYERS,
-                   "calls_per_step": len(prepared), "parallelism": f"replicas{world}",
-                   "l2": "inputs > L2: 0.97 GB resident int8 weights streamed per step"},
+        "config": step_config(m, world, len(prepared)),
         "roofline": roof,
         "pp128": short,
         "e2e": e2e,
@@ -562,6 +566,7 @@ def cpu_baseline(weights, acts, m, budget_s=10.0):
     workload (the first CPU_SAMPLE_ROWS tokens of each) until the time budget
     is spent; scaled by int8 ops to tok/s of a whole step."""
     import oracle
+    oracle.set_threads(oracle.host_threads())
     prepared = []
     for key, blocks in list(weights.items())[:8]:  # two layers' worth of calls
         _, members, k = layer_plan(key[0])[["qkv", "o", "gate_up", "down"].index(key[1])]
@@ -593,15 +598,31 @@ def cpu_baseline(weights, acts, m, budget_s=10.0):
                       f"int8 ops to one {LAYERS}-layer step"}
 
 
+def step_config(m: int, world: int, calls: int) -> dict:
+    """The `config` of a model-workload line, the same dict in both arms: N
+    replicas of one m-token prompt (N = world)."""
+    wbytes = sum(sum(n for _, n in members) * k for layer in range(LAYERS) for _, members, k in layer_plan(layer))
+    return {"workload": workload_name(m), "tokens_per_step": m, "global_batch": world * m, "seq_len": m,
+            "layers": LAYERS, "calls_per_step": calls, "parallelism": f"replicas{world}",
+            "l2": f"inputs > L2: {wbytes / 1e9:.2f} GB resident int8 weights streamed per step"}
+
+
 def run_reference(args, rank: int, world: int):
     """--impl reference: the reference's CPU implementation of the path (the
-    oracle port; the Rust reference has no toolchain here) on the host cores."""
+    oracle port; the Rust reference has no toolchain here) on every host
+    thread this process may use (the OMP_NUM_THREADS=1 that torchrun exports
+    is overridden).  Its inputs come from the oracle's own generator, byte for
+    byte those of our arm, so this process never loads librocknpu.so.  A step
+    is the same job as our arm's step at this world size: `world` replicas of
+    the whole workload (every layer's MUL_MAT calls over all m tokens); on N
+    GPUs rank 0 alone runs it on the host and the other ranks exit."""
     if rank != 0:
         return None
     import oracle
+    oracle.set_threads(oracle.host_threads())
     m = args.tokens
-    weights = make_weights()
-    acts = make_activations(m, seed=5000)
+    weights = make_weights(gen=oracle)
+    acts = make_activations(m, seed=5000, gen=oracle)
     # prepared once (the reference caches prepared weights), like our arm
     prepared = []
     for key, blocks in weights.items():
@@ -612,11 +633,12 @@ def run_reference(args, rank: int, world: int):
             ws.append(w)
             ss.append(s)
         prepared.append((key, np.concatenate(ws), np.concatenate(ss), k))
-    # each step is the whole workload: every layer's MUL_MAT calls over all
-    # m tokens (quantize + exact int32 GEMM + rescale, VNNI, all host threads)
+
+    # each replica: quantize + exact int32 GEMM + rescale of every call
     def step():
-        for key, w, s, k in prepared:
-            oracle.matmul_w8a8(w, s, acts[key])
+        for _ in range(world):
+            for key, w, s, k in prepared:
+                oracle.matmul_w8a8(w, s, acts[key])
 
     for _ in range(args.warmup):
         step()
@@ -624,19 +646,20 @@ def run_reference(args, rank: int, world: int):
     for _ in range(args.steps):
         step()
     step_s = (time.perf_counter() - t0) / args.steps
-    value = round(m / step_s, 2)
+    value = round(world * m / step_s, 2)
     line = {
         "impl": "reference",
         "metric": metric_name(m),
         "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(step_s * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int8 (W8A8, int32 accumulate, f32 out)", "data": "synthetic",
-        "config": {"workload": workload_name(m), "tokens_per_step": m,
-                   "seq_len": m, "layers": LAYERS},
+        "dtype": "int8 (W8A8, int32 accumulate, f32 out)",
+        "data": "synthetic (random-init N(0,0.02^2) -> Q4_K/Q6_K weights, N(0,1) activations)",
+        "config": step_config(m, world, len(prepared)),
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": oracle.threads(), "kind": "port",
                          "sample": f"each step runs all {len(prepared)} MUL_MAT calls of the {LAYERS} layers on "
-                                   f"{m} tokens (quantize + int32 GEMM on {oracle.gemm_path(m, HIDDEN, HIDDEN)} + "
-                                   "rescale on prepared weights)"},
+                                   f"{m} tokens, {world} time(s) (one per replica; the replicas reuse replica 0's "
+                                   f"activations), quantize + int32 GEMM on {oracle.gemm_path(m, HIDDEN, HIDDEN)} + "
+                                   "rescale on prepared weights"},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     return line

@@ -22,10 +22,9 @@ BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210}
 
 def build(force: bool = False) -> str:
     """Compile liboracle.so with the committed Makefile (gcc, OpenMP)."""
-    src = os.path.join(_HERE, "oracle.c")
+    srcs = [os.path.join(_HERE, f) for f in ("oracle.c", "synth.c", "oracle.h", "Makefile")]
     stale = (not os.path.exists(_LIB_PATH)
-             or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src)
-             or os.path.getmtime(_LIB_PATH) < os.path.getmtime(os.path.join(_HERE, "oracle.h")))
+             or any(os.path.getmtime(_LIB_PATH) < os.path.getmtime(s) for s in srcs))
     if force or stale:
         subprocess.run(["make", "-s", "-C", _HERE, "-B" if force else "liboracle.so"],
                        check=True)
@@ -79,6 +78,12 @@ def lib():
         L.orc_split_blocks.argtypes = [S, S, S, P, P]
         L.orc_threads.restype = ctypes.c_int
         L.orc_threads.argtypes = []
+        L.orc_set_threads.restype = None
+        L.orc_set_threads.argtypes = [ctypes.c_int]
+        L.orc_synth_normal.restype = None
+        L.orc_synth_normal.argtypes = [ctypes.c_uint64, ctypes.c_uint64, S, ctypes.c_float, P]
+        L.orc_synth_encode.restype = ctypes.c_int
+        L.orc_synth_encode.argtypes = [ctypes.c_uint32, P, S, S, P]
         _lib = L
     return _lib
 
@@ -90,6 +95,45 @@ def _p(a: np.ndarray):
 
 def threads() -> int:
     return int(lib().orc_threads())
+
+
+def set_threads(n: int) -> None:
+    """OpenMP threads of the oracle's parallel loops from now on."""
+    lib().orc_set_threads(int(n))
+
+
+def host_threads() -> int:
+    """Every hardware thread this process may run on (its CPU affinity set),
+    whatever OMP_NUM_THREADS the launcher exported."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def synth_normal(seed: int, count: int, sigma: float = 1.0, first: int = 0) -> np.ndarray:
+    """Seeded N(0, sigma^2) f32 values, the same as the library's
+    rocknpu_synth_normal."""
+    out = np.empty(count, dtype=np.float32)
+    lib().orc_synth_normal(seed, first, count, sigma, _p(out))
+    return out
+
+
+def synth_encode(kind: int, values: np.ndarray) -> np.ndarray:
+    """Rows of f32 values [n, k] as K-quant superblocks (flat uint8), the same
+    bytes as the library's rocknpu_synth_encode."""
+    values = np.ascontiguousarray(values, dtype=np.float32)
+    n, k = values.shape
+    out = np.empty(n * (k // 256) * BLOCK_BYTES[kind], dtype=np.uint8)
+    if lib().orc_synth_encode(kind, _p(values), k, n, _p(out)) != 0:
+        raise ValueError("synth_encode: k must be a multiple of 256")
+    return out
+
+
+def synth_q_weights(kind: int, n: int, k: int, seed: int, sigma: float = 0.02) -> np.ndarray:
+    """Seeded N(0, sigma^2) weights [n, k] encoded as K-quant blocks, the same
+    bytes as rocknpu_b200.synth_q_weights."""
+    return synth_encode(kind, synth_normal(seed, n * k, sigma).reshape(n, k))
 
 
 def dequant(kind: int, blocks: np.ndarray) -> np.ndarray:

@@ -78,6 +78,14 @@ size_t orc_split_blocks(size_t blocks, size_t block_width, size_t workers, size_
                         size_t *widths);
 
 int orc_threads(void);
+/* OpenMP threads for the calls that follow (threads > 0). */
+void orc_set_threads(int threads);
+
+/* Synthetic workload inputs (synth.c): N(0, sigma^2) values (value i of a
+ * seed depends only on first + i) and min/max K-quant encoders, byte for byte
+ * the library's rocknpu_synth_normal / rocknpu_synth_encode. */
+void orc_synth_normal(uint64_t seed, uint64_t first, size_t count, float sigma, float *out);
+int orc_synth_encode(uint32_t kind, const float *values, size_t k, size_t n, uint8_t *blocks);
 
 #ifdef __cplusplus
 }

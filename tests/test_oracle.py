@@ -202,3 +202,24 @@ def test_gemm_fast_path_equals_scalar_loops(monkeypatch, path, m, k, n):
     slow = oracle.gemm_i8_i32(a, w)
     assert np.array_equal(fast, slow)
     assert np.array_equal(fast, (a.astype(np.int64) @ w.astype(np.int64).T).astype(np.int32))
+
+
+@pytest.mark.parametrize("kind", [4, 5, 6])
+def test_oracle_synth_equals_library_synth(kind):
+    """The reference arm of bench.py builds its inputs with the oracle's own
+    generator (so that its process never loads librocknpu.so); the values and
+    K-quant block bytes must be the ones the library's generator gives the
+    B200 arm.  Sizes span the parallel and the serial split of both."""
+    import rocknpu_b200 as rk
+    for seed, first, count in ((0, 0, 1), (7, 12345, 4097), (1000, 3 * 2048, 256 * 2048)):
+        a = oracle.synth_normal(seed, count, 0.02, first=first)
+        b = rk.synth_normal(seed, count, 0.02, first=first)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    for n, k in ((1, 256), (33, 512), (256, 2048)):
+        vals = rk.synth_normal(kind * 100 + n, n * k, 0.02).reshape(n, k)
+        assert np.array_equal(oracle.synth_encode(kind, vals), rk.synth_encode(kind, vals))
+    # wide values (larger scales, clamped codes) and all-zero rows
+    wide = rk.synth_normal(99, 64 * 256, 3.0).reshape(64, 256)
+    wide[5] = 0.0
+    assert np.array_equal(oracle.synth_encode(kind, wide), rk.synth_encode(kind, wide))
+    assert np.array_equal(oracle.synth_q_weights(kind, 40, 1024, seed=3), rk.synth_q_weights(kind, 40, 1024, seed=3))
