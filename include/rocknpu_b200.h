@@ -13,6 +13,10 @@
  *     (NULL = the context's own stream) and the call returns without
  *     waiting.  Kernels report errors in the device word `status`
  *     (0 = ok, 1 = non-finite input, >1 = a device-side wait ran out).
+ *     Whenever that word is non-zero after the work has run, the call's
+ *     outputs are unspecified (later kernels of the call may have run on
+ *     scratch the failed step never wrote); only a zero status vouches for
+ *     them.
  *  3. Multi-GPU N-sharding: the row split, the all-gather layout, and peer
  *     (CUDA IPC) buffers for a GEMM whose epilogue all-gathers over NVLink.
  *  4. W8 sidecar files: the plugin's disk cache of prepared int8 weights.
@@ -148,12 +152,16 @@ int rocknpu_b200_matmul_w8a8(rocknpu_context *context, const float *a, const int
  * cudaFree or allocating library routine: the int8 activations, per-token
  * scales and split-K sums live in a 16 MiB array inside the library's device
  * memory, which every GPU that loads the library holds until the process
- * exits.  Limit: m * round_up(k, 16) + 4 * m (each rounded up to 256 bytes)
- * must fit in those 16 MiB, e.g. m = 2047 at k = 8192; larger calls return
- * ROCKNPU_STATUS_INVALID_ARGUMENT and print the sizes to stderr.
+ * exits.  Limits: k must be a multiple of 16, and m * k + 4 * m (each
+ * rounded up to 256 bytes) must fit in those 16 MiB, e.g. m = 2047 at
+ * k = 8192; other calls return ROCKNPU_STATUS_INVALID_ARGUMENT before any
+ * work is queued (oversized ones also print the sizes to stderr).
  * All pointers are device pointers on the current device; `status` (device,
  * one int) is cleared by the call and set by the kernels like the other
- * device entry points' status words.  Work is queued on `stream` and the
+ * device entry points' status words.  When *status is non-zero after the
+ * work has run (a non-finite activation, a device wait that ran out), the
+ * contents of `out` are unspecified: they may come from another call's
+ * leftovers in the shared array.  Work is queued on `stream` and the
  * call returns without waiting.  The first call on a device looks up the
  * array's device address (cudaGetSymbolAddress) with that device current;
  * make that first call before any stream capture.  Every call on a device

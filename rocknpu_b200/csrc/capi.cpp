@@ -14,6 +14,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -245,7 +246,7 @@ struct RockNpuContext {
     int* d_status = nullptr;  // device error word
     int* h_status = nullptr;  // pinned mirror
 
-    DevBuf a_f32, a_i8, a_scale, a_f16, out_f32, staging, swiglu_tmp;
+    DevBuf a_f32, a_i8, a_scale, a_f16, out_f32, staging;
     DevBuf gemm_ws;      // split-K workspace, all-zero between launches
     DevBuf quant_sync;   // fused-quantiser counters, all-zero between launches
     DevBuf hilo_a, hilo_out;  // HILO stacked activations [2m][k], summed outputs
@@ -1014,7 +1015,7 @@ void rocknpu_context_destroy(rocknpu_context* context) {
     c->decode.clear();
     c->decode_groups.clear();
     c->f16.clear();
-    for (DevBuf* b : {&c->a_f32, &c->a_i8, &c->a_scale, &c->a_f16, &c->out_f32, &c->staging, &c->swiglu_tmp,
+    for (DevBuf* b : {&c->a_f32, &c->a_i8, &c->a_scale, &c->a_f16, &c->out_f32, &c->staging,
                       &c->gemm_ws, &c->quant_sync, &c->hilo_a, &c->hilo_out})
         b->release();
     if (c->d_status) cudaFree(c->d_status);
@@ -1298,23 +1299,20 @@ int rocknpu_matmul_w8a8_swiglu_down_f32(rocknpu_context* context, const int8_t* 
         return kInvalid;
     size_t t;
     if (mul_overflows(projection_k, ffn_n, &t) || mul_overflows(ffn_n, output_n, &t)) return kInvalid;
-    std::vector<float> gate(ffn_n), up(ffn_n), act(ffn_n);
+    std::vector<float> gate(ffn_n), up(ffn_n);
     int st = rocknpu_matmul_w8a8_pair_f32_f32_m1(context, gw, gs, ffn_n, uw, us, ffn_n, a, gate.data(), up.data(),
                                                  projection_k);
     if (st != kOk) return st;
-    // f32 SwiGLU on the GPU (L:4368-4373)
-    if (!bind(context)) return kDeviceError;
-    if (context->swiglu_tmp.ensure(3 * ffn_n * sizeof(float))) return kExecError;
-    float* g = context->swiglu_tmp.as<float>();
-    if (cudaMemcpyAsync(g, gate.data(), ffn_n * 4, cudaMemcpyHostToDevice, context->stream) ||
-        cudaMemcpyAsync(g + ffn_n, up.data(), ffn_n * 4, cudaMemcpyHostToDevice, context->stream))
-        return kExecError;
-    rk::launch_swiglu(g, g + ffn_n, g + 2 * ffn_n, static_cast<int>(ffn_n), context->stream);
-    if (cudaGetLastError() ||
-        cudaMemcpyAsync(act.data(), g + 2 * ffn_n, ffn_n * 4, cudaMemcpyDeviceToHost, context->stream) ||
-        cudaStreamSynchronize(context->stream))
-        return kExecError;
-    return rocknpu_matmul_w8a8_f32_f32_m1(context, dw, ds, act.data(), out, ffn_n, output_n);
+    // F32 SwiGLU on the host, where the reference computes it (L:4368-4373):
+    // g * (1 / (1 + exp(-g))) * u with the C library's expf -- the function
+    // Rust's f32::exp calls -- and no fused multiply-add, so the down
+    // projection sees the reference's activation bits.
+    for (size_t i = 0; i < ffn_n; ++i) {
+        const float g = gate[i];
+        const float sig = 1.0f / (1.0f + ::expf(-g));
+        gate[i] = g * sig * up[i];
+    }
+    return rocknpu_matmul_w8a8_f32_f32_m1(context, dw, ds, gate.data(), out, ffn_n, output_n);
 }
 
 

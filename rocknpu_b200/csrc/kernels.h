@@ -112,8 +112,6 @@ void launch_hilo_residual(const float* a, int m, int k, long long lda, float* re
                           cudaStream_t s);
 void launch_add_halves(const float* hi, const float* lo, float* out, long long len, cudaStream_t s);
 
-// SwiGLU between the M=1 gate/up and down projections.
-void launch_swiglu(const float* gate, const float* up, float* out, int n, cudaStream_t s);
 
 int sm_count();
 

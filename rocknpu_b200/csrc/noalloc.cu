@@ -55,17 +55,19 @@ unsigned char* scratch_for_current_device() {
 
 extern "C" int rocknpu_b200_matmul_w8a8_noalloc(const float* a, const int8_t* w_i8, const float* w_scales, float* out,
                                                 size_t m, size_t k, size_t n, int* status, rocknpu_stream stream) {
+    // k % 16: the int8 rows are read by the GEMV in 16-byte vectors and by
+    // the GEMM's tensor maps with a k-byte weight pitch (multiples of 16)
     if (!a || !w_i8 || !w_scales || !out || !status || m == 0 || k == 0 || n == 0 || m > 0x7fffffff ||
-        n > 0x7fffffff || k > 0x7fffffff)
+        n > 0x7fffffff || k > 0x7fffffff || k % 16 != 0)
         return ROCKNPU_STATUS_INVALID_ARGUMENT;
-    const size_t ld8 = (k + 15) / 16 * 16;
+    const size_t ld8 = k;
     const size_t scales_off = 0;
     const size_t a8_off = align256(m * sizeof(float));
     const size_t needed = a8_off + align256(m * ld8);
     if (needed > kScratchBytes) {
         std::fprintf(stderr,
                      "rocknpu_b200_matmul_w8a8_noalloc: m=%zu, k=%zu needs %zu bytes of scratch; the fixed scratch "
-                     "holds %zu (m * round_up(k, 16) + 4 * m, rounded to 256-byte blocks)\n",
+                     "holds %zu (m * k + 4 * m, each rounded up to 256 bytes)\n",
                      m, k, needed, kScratchBytes);
         return ROCKNPU_STATUS_INVALID_ARGUMENT;
     }
@@ -79,7 +81,7 @@ extern "C" int rocknpu_b200_matmul_w8a8_noalloc(const float* a, const int8_t* w_
     rk::launch_quant_rows(a, static_cast<int>(m), static_cast<int>(k), static_cast<long long>(k), a8,
                           static_cast<long long>(ld8), a_scales, status, s);
     if (cudaGetLastError() != cudaSuccess) return ROCKNPU_STATUS_EXECUTION_ERROR;
-    if (m == 1 && k % 16 == 0) {
+    if (m == 1) {
         rk::launch_gemv_w8a8(w_i8, w_scales, a8, a_scales, static_cast<int>(k), static_cast<int>(n), out, s);
         return cudaGetLastError() == cudaSuccess ? ROCKNPU_STATUS_OK : ROCKNPU_STATUS_EXECUTION_ERROR;
     }

@@ -437,17 +437,6 @@ __global__ void f32_to_f16_kernel(const float* __restrict__ a, int m, int k, lon
     }
 }
 
-// F32 SwiGLU (capi/src/lib.rs:4368-4373): g * (1 / (1 + exp(-g))) * u.
-__global__ void swiglu_kernel(const float* __restrict__ gate, const float* __restrict__ up, float* __restrict__ out,
-                              int n) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) {
-        const float g = gate[i];
-        const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
-        out[i] = __fmul_rn(__fmul_rn(g, sig), up[i]);
-    }
-}
-
 template <class F>
 void set_smem(F* f, size_t bytes) {
     // dynamic + static shared memory above 48 KB needs the opt-in
@@ -529,10 +518,6 @@ void launch_hilo_residual(const float* a, int m, int k, long long lda, float* re
 void launch_add_halves(const float* hi, const float* lo, float* out, long long len, cudaStream_t s) {
     const int blocks = static_cast<int>(std::min<long long>((len + 255) / 256, 148LL * 16));
     add_halves_kernel<<<std::max(blocks, 1), 256, 0, s>>>(hi, lo, out, len);
-}
-
-void launch_swiglu(const float* gate, const float* up, float* out, int n, cudaStream_t s) {
-    swiglu_kernel<<<(n + 255) / 256, 256, 0, s>>>(gate, up, out, n);
 }
 
 }  // namespace rk

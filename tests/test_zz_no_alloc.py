@@ -32,7 +32,12 @@ def _with_context(ctx, a, w, s, out, stream):
                                              k, n, stream)
 
 
-@pytest.mark.parametrize("m,k,n", [(128, 2048, 5632), (77, 5632, 256), (1, 2048, 512), (512, 2048, 2048)])
+# (336, 49152, 256): the tile plan splits K (few output tiles, long K), but
+# the int32 partial sums do not fit beside the 15.75 MiB of int8 activations
+# in the 16 MiB array, so this call takes the branch that runs the GEMM
+# without K splits.
+@pytest.mark.parametrize("m,k,n", [(128, 2048, 5632), (77, 5632, 256), (1, 2048, 512), (512, 2048, 2048),
+                                   (336, 49152, 256)])
 def test_noalloc_matches_context_entry_point_twice(m, k, n):
     rng = np.random.default_rng(m * 7 + n)
     stream = torch.cuda.current_stream().cuda_stream
@@ -53,9 +58,28 @@ def test_noalloc_matches_context_entry_point_twice(m, k, n):
             assert torch.equal(got.view(torch.int32), ref.view(torch.int32)), f"call {call} differs"
 
 
+def test_noalloc_no_split_branch_is_reached():
+    """The shape above splits K in the context path (it has a workspace) and
+    its partial sums would overflow the fixed array."""
+    m, k, n = 336, 49152, 256
+    ws = rk.lib().rocknpu_b200_gemm_workspace_bytes(m, n, k)
+    assert ws > 0 and ws > (16 << 20) - (m * k + 4 * m)
+
+
 def test_noalloc_rejects_oversize_and_flags_non_finite():
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     stream = torch.cuda.current_stream().cuda_stream
+    # k not a multiple of 16: rejected before any work is queued, so the
+    # status word keeps the value it had
+    status.fill_(5)
+    a = torch.ones((3, 200), device="cuda")
+    w = torch.ones((64, 200), dtype=torch.int8, device="cuda")
+    s = torch.ones(64, device="cuda")
+    out = torch.empty((3, 64), device="cuda")
+    assert _noalloc(a, w, s, out, status, stream) == rk.STATUS_INVALID_ARGUMENT
+    torch.cuda.synchronize()
+    assert status.item() == 5
+    status.zero_()
     k, n = 8192, 128
     w = torch.zeros((n, k), dtype=torch.int8, device="cuda")
     s = torch.ones(n, device="cuda")
