@@ -27,13 +27,25 @@ weight cache), 1.0 GB per step > L2, so no extra L2 flush is needed.
   "sample" names the path), rescale -- timed on a bounded sample of the same
   workload.
 
+* pp128.roofline / roofline: the step's GEMM launches alone (one graph),
+  algorithmic bytes and int8 ops against the measured peaks.
+* cfg5 (N = 1): BASELINE.json configs[4] beside the headline step -- the
+  W8A8 GEMM of the Q4_K weight N=28672 x K=8192 at M in {128, 1024, 4096,
+  16384} (whole job and the GEMM kernel alone, against the int8 tensor or
+  HBM roofline) and the M = 1 decode GEMVs on the same weight.
+* shard (N > 1): the same GEMMs N-sharded over the ranks, the output columns
+  all-gathered over NVLink by the GEMM epilogue's peer stores (strong
+  scaling), with the per-rank receive bound and an in-run bit check of
+  sampled rows against a single-GPU GEMM on rank 0.
+
 Other configs: --workload llama32-1b (configs[2], pp512) and qwen25-1.5b
 (configs[3], pp2048) replay those models' MUL_MAT calls the same way;
---workload cfg5 is the large-GEMM sharding sweep.
+--workload cfg5 is the large-GEMM sharding sweep as its own line.
 
-Multi-GPU (torchrun): the path does not shard at this size, so each rank
-runs its own replica on its own prompt batch (weak scaling, no collective);
-value = all ranks' tokens / max-over-ranks time.
+Multi-GPU (torchrun): the per-layer GEMMs do not shard at this size, so each
+rank runs its own replica of the headline step on its own prompt batch (weak
+scaling, no collective); value = all ranks' tokens / max-over-ranks time.
+The large cfg5 GEMMs do shard (the `shard` key above).
 """
 from __future__ import annotations
 
@@ -389,6 +401,61 @@ def run_ours(args, rank: int, world: int):
     if rk.lib().rocknpu_b200_context_check(ctx.handle) != 0:
         raise RuntimeError("device status error during timing")
 
+    # roofline of the dominant kernel (K3): the step's GEMM launches alone,
+    # on pre-quantised activations, as one graph
+    def gemm_roofline(mm, acts_src, outs_src, step_ms):
+        a8 = {key: dev.quantize_rows(acts_src[key], status) for key in prepared}
+        ws_bytes = max(dev.workspace_bytes(mm, w8.shape[0], k) for (w8, s8, k) in prepared.values())
+        gemm_ws = dev.new_workspace(ws_bytes)
+
+        def gemm_step():
+            for key, (w8, s8, k) in prepared.items():
+                dev.gemm_w8a8(a8[key][0], a8[key][1], w8, s8, status, out=outs_src[key[1]], workspace=gemm_ws)
+
+        gemm_step()
+        torch.cuda.synchronize()
+        g2 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g2):
+            gemm_step()
+        for _ in range(3):
+            g2.replay()
+        reps = max(5, args.steps)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            g2.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        assert status.item() == 0, "GEMM status error"
+        gemm_ms = e0.elapsed_time(e1) / reps
+        if dist is not None:
+            t = torch.tensor([gemm_ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            gemm_ms = float(t.item())
+        alg_bytes, alg_ops = algorithmic(mm)
+        gb_s = alg_bytes / (gemm_ms * 1e-3) / 1e9
+        tops = alg_ops / (gemm_ms * 1e-3) / 1e12
+        t_hbm = alg_bytes / (hbm_peak * 1e9)
+        t_tc = alg_ops / (int8_peak_tops * 1e12)
+        if t_hbm >= t_tc:
+            r = {"bound": "hbm", "achieved": round(gb_s, 1), "peak": hbm_peak, "unit": "GB/s",
+                 "frac": round(gb_s / hbm_peak, 4)}
+        else:
+            r = {"bound": "tensor", "achieved": round(tops, 1), "peak": int8_peak_tops, "unit": "TOP/s",
+                 "frac": round(tops / int8_peak_tops, 4)}
+        traffic = profiled_traffic(mm)
+        r.update({"kernel": "gemm_tc_kernel (K3, tcgen05 kind::i8)", "traffic": traffic,
+                  "traffic_unit": f"DRAM bytes per step ({len(prepared)} launches), ncu capture" if traffic else None,
+                  "peak_source": f"{peak_src} (int8 = 2 x bf16_tflops)" if r["bound"] == "tensor"
+                  else f"{peak_src} hbm_gbs",
+                  "hbm_frac": round(gb_s / hbm_peak, 4), "tensor_frac": round(tops / int8_peak_tops, 4),
+                  "gemm_ms_per_step": round(gemm_ms, 4), "gemm_share_of_step": round(gemm_ms / step_ms, 3),
+                  "gemm_launches_per_step": len(prepared),
+                  "algorithmic_bytes_per_step": alg_bytes, "int8_ops_per_step": alg_ops})
+        del g2
+        return r
+
     # the other prompt length of the headline metric (pp128 beside pp512):
     # the same calls on the first 128 tokens of every activation
     short = None
@@ -422,57 +489,11 @@ def run_ours(args, rank: int, world: int):
             t = torch.tensor([t_short], device="cuda")
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             t_short = float(t.item())
-        short = {"tokens_per_step": ms_short, "value": round(world * ms_short / (t_short * 1e-3), 1), "unit": "tok/s",
-                 "ms_per_step": round(t_short, 4)}
         del gs
+        short = {"tokens_per_step": ms_short, "value": round(world * ms_short / (t_short * 1e-3), 1), "unit": "tok/s",
+                 "ms_per_step": round(t_short, 4), "roofline": gemm_roofline(ms_short, s_acts, s_outs, t_short)}
 
-    # roofline of the dominant kernel (K3): the step's 88 GEMM launches alone,
-    # on pre-quantised activations, as one graph
-    a8 = {key: dev.quantize_rows(d_acts[key], status) for key in prepared}
-    ws_bytes = max(dev.workspace_bytes(m, w8.shape[0], k) for (w8, s8, k) in prepared.values())
-    gemm_ws = dev.new_workspace(ws_bytes)
-
-    def gemm_step():
-        for key, (w8, s8, k) in prepared.items():
-            dev.gemm_w8a8(a8[key][0], a8[key][1], w8, s8, status, out=outs[key[1]], workspace=gemm_ws)
-
-    gemm_step()
-    torch.cuda.synchronize()
-    g2 = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g2):
-        gemm_step()
-    for _ in range(3):
-        g2.replay()
-    reps = max(5, args.steps)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    e0.record()
-    for _ in range(reps):
-        g2.replay()
-    e1.record()
-    torch.cuda.synchronize()
-    assert status.item() == 0, "GEMM status error"
-    gemm_ms = e0.elapsed_time(e1) / reps
-    alg_bytes, alg_ops = algorithmic(m)
-    gb_s = alg_bytes / (gemm_ms * 1e-3) / 1e9
-    tops = alg_ops / (gemm_ms * 1e-3) / 1e12
-    t_hbm = alg_bytes / (hbm_peak * 1e9)
-    t_tc = alg_ops / (int8_peak_tops * 1e12)
-    if t_hbm >= t_tc:
-        roof = {"bound": "hbm", "achieved": round(gb_s, 1), "peak": hbm_peak, "unit": "GB/s",
-                "frac": round(gb_s / hbm_peak, 4)}
-    else:
-        roof = {"bound": "tensor", "achieved": round(tops, 1), "peak": int8_peak_tops, "unit": "TOP/s",
-                "frac": round(tops / int8_peak_tops, 4)}
-    traffic = profiled_traffic(m)
-    roof.update({"kernel": "gemm_tc_kernel (K3, tcgen05 kind::i8)", "traffic": traffic,
-                 "traffic_unit": "DRAM bytes per step (88 launches), ncu capture" if traffic else None,
-                 "peak_source": f"{peak_src} (int8 = 2 x bf16_tflops)" if roof["bound"] == "tensor"
-                 else f"{peak_src} hbm_gbs",
-                 "hbm_frac": round(gb_s / hbm_peak, 4), "tensor_frac": round(tops / int8_peak_tops, 4),
-                 "gemm_ms_per_step": round(gemm_ms, 4), "gemm_share_of_step": round(gemm_ms / ms, 3),
-                 "gemm_launches_per_step": len(prepared),
-                 "algorithmic_bytes_per_step": alg_bytes, "int8_ops_per_step": alg_ops})
+    roof = gemm_roofline(m, d_acts, outs, ms)
 
     # e2e through the reference C ABI with page-locked host buffers
     e2e = None
@@ -523,6 +544,18 @@ def run_ours(args, rank: int, world: int):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
 
+    # BASELINE.json configs[4] beside the headline step: at N = 1 the large
+    # W8A8 GEMM (M in {128, 1024, 4096, 16384}) and the M = 1 decode GEMVs on
+    # the N=28672 x K=8192 Q4_K weight, against their rooflines; at N > 1 the
+    # same GEMMs N-sharded over the ranks with the output all-gathered over
+    # NVLink, checked bit for bit against one GPU in the run
+    big = big_clocks = None
+    if not args.no_cfg5 and MODEL == "tinyllama":
+        big, big_clocks = cfg5_block(list(CFG5_M), min(args.steps, 10), max(args.warmup, 3), rank, world,
+                                     route=args.route)
+        if big is not None:
+            big["clocks"] = big_clocks
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(weights, acts, m, budget_s=args.cpu_seconds)
@@ -553,6 +586,8 @@ def run_ours(args, rank: int, world: int):
         "clocks": clocks.summary(),
         "setup_s": round(gen_s, 1),
     }
+    if big is not None:
+        line["cfg5" if world == 1 else "shard"] = big
     return line
 
 
@@ -831,26 +866,56 @@ def cfg5_activations(m: int, device="cuda"):
     return x
 
 
-def run_cfg5(args, rank: int, world: int):
-    """W8A8 GEMM throughput of the N=28672 x K=8192 Q4_K weight, N-sharded over
-    the ranks (strong scaling: the same GEMMs whatever the GPU count), plus the
-    M=1 decode GEMV.  Per M, one step = K2 quantisation of X on every rank +
-    the rank's tcgen05 GEMM + the all-gather of the output columns (peer
-    stores fused into the epilogue, or NCCL), so that every rank holds Y."""
+def _timed(fn, steps, warmup, dist):
+    """Device time of `steps` calls after `warmup` (CUDA events on the current
+    stream, barrier and synchronize on both sides, max over ranks), ms."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+# Measured NVLink peer-copy rate per direction on this pool's B200s (GB/s):
+# the receive bound of the all-gather.
+PEER_GBS = 770.0
+
+
+def cfg5_block(ms_list, steps, warmup, rank, world, route="peer", check=True):
+    """BASELINE.json configs[4] on this process's GPU(s): the Q4_K weight
+    N=28672 x K=8192 N-sharded over the ranks (strong scaling: the same GEMMs
+    whatever the GPU count), per M one step = K2 quantisation of X on every
+    rank + the rank's tcgen05 GEMM + the all-gather of the output columns
+    (peer stores fused into the epilogue, or NCCL), so that every rank holds
+    Y; the local GEMM alone on pre-quantised X gives the kernel's roofline
+    fraction.  Plus the M=1 decode GEMV on the same weight.  With world > 1
+    and `check`, sampled rows of the gathered Y on every rank are compared
+    bit for bit with a single-GPU GEMM of the whole weight on rank 0.
+    Returns (result dict, clock summary) on rank 0, (None, None) elsewhere."""
     import torch
     import rocknpu_b200 as rk
     from rocknpu_b200 import device as dev
     from rocknpu_b200 import shard
 
-    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
     hbm_peak, bf16_peak, peak_src = load_peaks()
     int8_peak = 2.0 * bf16_peak
     dist = None
     if world > 1:
         import torch.distributed as dist
-    ms_list = [int(v) for v in args.m_list.split(",")]
     max_m = max(ms_list)
-
     t0 = time.time()
     rows = shard.shard_rows(CFG5_N, world)
     start, width = rows[rank]
@@ -859,70 +924,113 @@ def run_cfg5(args, rank: int, world: int):
     vals = rk.synth_normal(0, width * CFG5_K, 0.02, first=start * CFG5_K).reshape(width, CFG5_K)
     blocks = rk.synth_encode(4, vals)
     del vals
-    sm = shard.ShardedMatmul(4, blocks, CFG5_K, CFG5_N, route=args.route, max_m=max_m, blocks_are_local=True)
+    sm = shard.ShardedMatmul(4, blocks, CFG5_K, CFG5_N, route=route, max_m=max_m, blocks_are_local=True)
     gen_s = time.time() - t0
-
-    def timed(fn, steps, warmup):
-        for _ in range(warmup):
-            fn()
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(steps):
-            fn()
-        e1.record()
-        torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / steps
-        if dist is not None:
-            t = torch.tensor([ms], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
-
-    sweep = {}
-    head = None
-    with ClockSampler(torch.cuda.current_device()) as clocks:
+    res = {"n": CFG5_N, "k": CFG5_K, "weight": "Q4_K, N(0, 0.02^2) seed 0", "rows_per_rank": width,
+           "route": route if world > 1 else None, "setup_s": round(gen_s, 1), "gemm": {}}
+    clocks = ClockSampler(torch.cuda.current_device())
+    with clocks:
         clocks.mark("t_start")
         for m in ms_list:
             x = cfg5_activations(m)
-            out = None
-            ms = timed(lambda: sm(x), args.steps, args.warmup)
+            ms = _timed(lambda: sm(x), steps, warmup, dist)
             a8, a_s = sm.quantize(x)
             local = torch.empty((m, max(width, 1)), dtype=torch.float32, device="cuda")
-            gemm_ms = timed(lambda: dev.gemm_w8a8(a8, a_s, sm.w8, sm.w_scales, sm.status, out=local),
-                            args.steps, args.warmup)
+            gemm_ms = _timed(lambda: dev.gemm_w8a8(a8, a_s, sm.w8, sm.w_scales, sm.status, out=local),
+                             steps, warmup, dist)
             sm.check()
             ops = 2.0 * m * CFG5_N * CFG5_K
             local_ops = 2.0 * m * width * CFG5_K
             local_bytes = width * CFG5_K + m * CFG5_K + 4 * m * width + 4 * width + 4 * m
+            tops_local = local_ops / (gemm_ms * 1e-3) / 1e12
+            gbs_local = local_bytes / (gemm_ms * 1e-3) / 1e9
+            bound = "tensor" if local_ops / (int8_peak * 1e12) >= local_bytes / (hbm_peak * 1e9) else "hbm"
             r = {"ms_per_step": round(ms, 4), "tops": round(ops / (ms * 1e-3) / 1e12, 1),
-                 "gemm_ms_local": round(gemm_ms, 4),
-                 "gemm_tops_local": round(local_ops / (gemm_ms * 1e-3) / 1e12, 1),
-                 "gemm_tensor_frac": round(local_ops / (gemm_ms * 1e-3) / 1e12 / int8_peak, 4),
-                 "gemm_hbm_frac": round(local_bytes / (gemm_ms * 1e-3) / 1e9 / hbm_peak, 4),
-                 "exchange_bytes_per_rank": 4 * m * width * (world - 1)}
-            sweep[str(m)] = r
-            head = (m, r)
-            del x, a8, a_s, local, out
+                 "gemm_ms_local": round(gemm_ms, 4), "gemm_tops_local": round(tops_local, 1),
+                 "bound": bound,
+                 "frac": round(tops_local / int8_peak if bound == "tensor" else gbs_local / hbm_peak, 4),
+                 "tensor_frac": round(tops_local / int8_peak, 4), "hbm_frac": round(gbs_local / hbm_peak, 4)}
+            if world > 1:
+                recv = 4 * m * (CFG5_N - width)
+                recv_ms = recv / (PEER_GBS * 1e9) * 1e3
+                r.update({"recv_bytes_per_rank": recv, "recv_bound_ms": round(recv_ms, 4),
+                          "floor_ms": round(max(recv_ms, gemm_ms), 4),
+                          "job_vs_floor": round(max(recv_ms, gemm_ms) / ms, 4)})
+            res["gemm"][str(m)] = r
+            del x, a8, a_s, local
         # M = 1 decode GEMV (K5) over the same rows
         x1 = cfg5_activations(1)
-        gemv_ms = timed(lambda: sm(x1), max(args.steps, 20), args.warmup)
+        gemv_ms = _timed(lambda: sm(x1), max(steps, 20), warmup, dist)
         a8, a_s = sm.quantize(x1)
         o1 = torch.empty(max(width, 1), dtype=torch.float32, device="cuda")
-        gemv_local = timed(lambda: dev.gemv_w8a8(a8, a_s, sm.w8, sm.w_scales, out=o1), max(args.steps, 50),
-                           args.warmup)
+        gemv_local = _timed(lambda: dev.gemv_w8a8(a8, a_s, sm.w8, sm.w_scales, out=o1), max(steps, 50), warmup,
+                            dist)
         gbytes = width * CFG5_K + 8 * width + CFG5_K + 4
-        sweep["1"] = {"ms_per_step": round(gemv_ms, 4), "gemv_us_local": round(gemv_local * 1e3, 2),
-                      "gemv_gbs_local": round(gbytes / (gemv_local * 1e-3) / 1e9, 1),
-                      "gemv_hbm_frac": round(gbytes / (gemv_local * 1e-3) / 1e9 / hbm_peak, 4)}
+        res["gemv_w8"] = {"kernel": "gemv_w8a8_kernel (int8 rows, dp4a)", "ms_per_step": round(gemv_ms, 4),
+                          "us_local": round(gemv_local * 1e3, 2),
+                          "gbs_local": round(gbytes / (gemv_local * 1e-3) / 1e9, 1),
+                          "hbm_frac": round(gbytes / (gemv_local * 1e-3) / 1e9 / hbm_peak, 4),
+                          "bytes": gbytes}
         clocks.mark("t_end")
     sm.check()
+    if world > 1 and check:
+        res["bitexact"] = _cfg5_shard_check(sm, max_m, rank, world, dist)
     sm.close()
+    res["peak_source"] = f"{peak_src}: int8 = 2 x bf16_tflops {int8_peak:.0f} TOP/s, hbm_gbs {hbm_peak:.0f}"
+    if rank != 0:
+        return None, None
+    return res, clocks.summary()
+
+
+def _cfg5_shard_check(sm, m, rank, world, dist):
+    """Sampled rows of the all-gathered Y: identical bits on every rank, and
+    equal to a single-GPU GEMM of the whole weight on rank 0."""
+    import torch
+    import rocknpu_b200 as rk
+    from rocknpu_b200 import device as dev
+    x = cfg5_activations(m)
+    y = sm(x)
+    sample = torch.arange(0, m, max(1, m // 256), device="cuda")[:256]
+    ys = y.index_select(0, sample).contiguous()
+    sm.check()
+    h = ys.view(torch.int32).to(torch.int64)
+    sig = torch.stack([h.sum(), (h * torch.arange(1, h.shape[1] + 1, device="cuda")).sum()])
+    sigs = [torch.empty_like(sig) for _ in range(world)]
+    dist.all_gather(sigs, sig)
+    same_on_ranks = all(torch.equal(s_, sigs[0]) for s_ in sigs)
+    ok = torch.tensor([1], device="cuda")
+    if rank == 0:
+        vals = rk.synth_normal(0, CFG5_N * CFG5_K, 0.02).reshape(CFG5_N, CFG5_K)
+        blocks = torch.from_numpy(rk.synth_encode(4, vals)).cuda()
+        del vals
+        status = dev.new_status()
+        w8, ws = dev.prepare_w8(4, blocks, CFG5_K, CFG5_N, status)
+        xs = x.index_select(0, sample).contiguous()
+        a8, a_s = dev.quantize_rows(xs, status)
+        ref = torch.empty((xs.shape[0], CFG5_N), dtype=torch.float32, device="cuda")
+        dev.gemm_w8a8(a8, a_s, w8, ws, status, out=ref)
+        torch.cuda.synchronize()
+        ok[0] = int(status.item() == 0 and torch.equal(ref.view(torch.int32), ys.view(torch.int32)))
+        del blocks, w8, ws, ref
+    dist.broadcast(ok, 0)
+    return {"rows_checked": int(sample.numel()), "m": m, "same_on_every_rank": bool(same_on_ranks),
+            "equal_to_single_gpu": bool(ok.item()), "ok": bool(same_on_ranks and ok.item())}
+
+
+def run_cfg5(args, rank: int, world: int):
+    """--workload cfg5: the sweep of BASELINE.json configs[4] as its own line
+    (whole-job TOP/s at the largest M is the value)."""
+    import torch
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+    ms_list = [int(v) for v in args.m_list.split(",")]
+    res, clocks = cfg5_block(ms_list, args.steps, args.warmup, rank, world, route=args.route,
+                             check=not args.no_check)
     if rank != 0:
         return None
-    m, r = head
+    m = max(ms_list)
+    r = res["gemm"][str(m)]
+    hbm_peak, bf16_peak, peak_src = load_peaks()
+    int8_peak = 2.0 * bf16_peak
     line = {
         "metric": f"W8A8 GEMM TOPS (cfg5 Q4_K N={CFG5_N} K={CFG5_K}, M={m}, N-sharded, Y all-gathered)",
         "value": r["tops"], "unit": "TOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -932,16 +1040,15 @@ def run_cfg5(args, rank: int, world: int):
         "config": {"workload": "cfg5-large-gemm-sharding-sweep", "n": CFG5_N, "k": CFG5_K, "m_list": ms_list,
                    "parallelism": f"nshard{world}" + (f"-{args.route}" if world > 1 else ""),
                    "l2": "weights 235 MB int8 > L2 (streamed every step)"},
-        "roofline": {"bound": "tensor", "achieved": r["gemm_tops_local"], "peak": int8_peak, "unit": "TOP/s",
-                     "frac": r["gemm_tensor_frac"], "traffic": None,
-                     "kernel": "gemm_tc_kernel (K3, tcgen05 kind::i8), this rank's rows",
+        "roofline": {"bound": r["bound"], "achieved": r["gemm_tops_local"], "peak": int8_peak, "unit": "TOP/s",
+                     "frac": r["tensor_frac"], "traffic": None,
+                     "kernel": "gemm_tc_kernel / gemm_pair_kernel (K3, tcgen05 kind::i8), this rank's rows",
                      "peak_source": f"{peak_src} (int8 = 2 x bf16_tflops)"},
-        "sweep": sweep,
+        "sweep": res,
         "e2e": None,
         "cpu_baseline": None,
         "gpu_launches": None,
-        "clocks": clocks.summary(),
-        "setup_s": round(gen_s, 1),
+        "clocks": clocks,
     }
     return line
 
@@ -961,6 +1068,9 @@ def main():
     ap.add_argument("--route", choices=["peer", "allgather"], default="peer",
                     help="cfg5 output exchange at N > 1")
     ap.add_argument("--m-list", default=",".join(str(m) for m in CFG5_M))
+    ap.add_argument("--no-check", action="store_true", help="cfg5 at N > 1: skip the in-run bit check")
+    ap.add_argument("--no-cfg5", action="store_true",
+                    help="default workload: skip the cfg5 GEMM/GEMV block (N=1) or the sharded block (N>1)")
     ap.add_argument("--f16", action="store_true", help="model workloads through the FP16 executor (one GPU)")
     args = ap.parse_args()
     if args.workload in MODELS:

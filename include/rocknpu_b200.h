@@ -107,6 +107,27 @@ int rocknpu_b200_host_free(void *ptr);
  * rocknpu_b200_matmul_w8a8) into a status code, clearing it. */
 int rocknpu_b200_context_check(rocknpu_context *context);
 
+/* Prompt-path (M > 1) weight caches of a context: resident single
+ * projections and concatenated groups, the calls that found their prepared
+ * weights resident (hits) or prepared them (misses), and the bytes held.  The
+ * reference keeps the same caches (decode_mtile_weights,
+ * decode_mtile_concat_weights, capi/src/lib.rs:198-236) and counts them in its
+ * prompt-path profile (:3900-3996); this exposes them to callers and tests. */
+typedef struct rocknpu_b200_prompt_cache_stats {
+    size_t single_entries;
+    size_t group_entries;
+    size_t hits;
+    size_t misses;
+    size_t resident_bytes;
+} rocknpu_b200_prompt_cache_stats;
+int rocknpu_b200_context_prompt_cache_stats(const rocknpu_context *context, rocknpu_b200_prompt_cache_stats *out);
+
+/* The status code of a device status word, as the host-pointer entry points
+ * return it: 0 -> ROCKNPU_STATUS_OK, 1 (non-finite input) ->
+ * ROCKNPU_STATUS_INVALID_ARGUMENT, any other value (a device-side wait that
+ * ran out) -> ROCKNPU_STATUS_EXECUTION_ERROR. */
+int rocknpu_b200_status_code(int device_status);
+
 /* K1: Q4_K/Q5_K/Q6_K rows (kind 4/5/6, n rows of k values, k % 256 == 0) ->
  * int8 rows w_i8[n][k] + scales[n], bit-identical to the reference's
  * prepare_q*_k_w8a8 (capi/src/lib.rs:711-757, 974-994). */
@@ -221,6 +242,12 @@ void *rocknpu_b200_peer_buffer_ptr(rocknpu_b200_peer_buffer *buffer, int r);
  * after it.  Waits are bounded (2 s); a rank that never arrives leaves
  * status 6 in *status. */
 int rocknpu_b200_peer_barrier(rocknpu_b200_peer_buffer *buffer, int *status, rocknpu_stream stream);
+/* Wait limit of the peer barrier's flag spin for the barriers queued after
+ * this call, in milliseconds (1 .. 600000; 0 restores the 2 s default).  The
+ * reference bounds its NPU completion wait the same way
+ * (rocknpu-matmul/src/int8_decode.rs:13).  A short limit lets a caller (or a
+ * test) learn quickly that a rank will not arrive. */
+int rocknpu_b200_set_peer_wait_limit_ms(uint32_t ms);
 void rocknpu_b200_peer_buffer_destroy(rocknpu_b200_peer_buffer *buffer);
 
 /* K3 with the all-gather fused into the epilogue: this rank's n_local weight

@@ -62,6 +62,8 @@ SIGNATURES = {
     "rocknpu_mul_mat_supported": (_I, [_P]),
     "rocknpu_b200_context_stream": (_P, [_P]),
     "rocknpu_b200_context_check": (_I, [_P]),
+    "rocknpu_b200_status_code": (_I, [_I]),
+    "rocknpu_b200_context_prompt_cache_stats": (_I, [_P, _P]),
     "rocknpu_b200_host_mapped": (_I, [_P, _S]),
     "rocknpu_b200_host_alloc": (_P, [_S]),
     "rocknpu_b200_host_free": (_I, [_P]),
@@ -80,6 +82,7 @@ SIGNATURES = {
     "rocknpu_b200_peer_buffer_open": (_I, [_P, _P]),
     "rocknpu_b200_peer_buffer_ptr": (_P, [_P, _I]),
     "rocknpu_b200_peer_barrier": (_I, [_P, _P, _P]),
+    "rocknpu_b200_set_peer_wait_limit_ms": (_I, [_U32]),
     "rocknpu_b200_peer_buffer_destroy": (None, [_P]),
     "rocknpu_b200_gemm_w8a8_gather": (_I, [_P, _S, _P, _P, _S, _P, _P, _S, _S, _S, _S, _S, _S, _P, _P]),
     "rocknpu_b200_source_fingerprint": (ctypes.c_uint64, [_P, _S]),
@@ -97,6 +100,12 @@ class CacheStats(ctypes.Structure):
     _fields_ = [("hits", _S), ("misses", _S), ("entries", _S), ("resident_bytes", _S),
                 ("hit_ns", ctypes.c_uint64), ("miss_ns", ctypes.c_uint64), ("tuned_shapes", _S),
                 ("worker1_calls", _S), ("worker2_calls", _S), ("worker3_calls", _S), ("ksplit_calls", _S)]
+
+
+class PromptCacheStats(ctypes.Structure):
+    """rocknpu_b200_prompt_cache_stats."""
+    _fields_ = [("single_entries", _S), ("group_entries", _S), ("hits", _S), ("misses", _S),
+                ("resident_bytes", _S)]
 
 
 class MulMatDesc(ctypes.Structure):
@@ -234,6 +243,13 @@ class Context:
         st = self._lib.rocknpu_context_decode_cache_stats(self.handle, ctypes.byref(s))
         if st != 0:
             raise RuntimeError(f"decode_cache_stats status {st}")
+        return s
+
+    def prompt_cache_stats(self) -> PromptCacheStats:
+        s = PromptCacheStats()
+        st = self._lib.rocknpu_b200_context_prompt_cache_stats(self.handle, ctypes.byref(s))
+        if st != 0:
+            raise RuntimeError(f"prompt_cache_stats status {st}")
         return s
 
     def set_overlap(self, fn) -> int:

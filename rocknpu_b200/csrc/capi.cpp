@@ -1324,6 +1324,23 @@ rocknpu_stream rocknpu_b200_context_stream(rocknpu_context* context) {
 
 int rocknpu_b200_host_mapped(const void* ptr, size_t bytes) { return host_mapped(ptr, bytes) ? 1 : 0; }
 
+int rocknpu_b200_context_prompt_cache_stats(const rocknpu_context* context, rocknpu_b200_prompt_cache_stats* out) {
+    if (!context || !out) return kInvalid;
+    *out = rocknpu_b200_prompt_cache_stats{};
+    out->single_entries = context->mtile.size();
+    out->group_entries = context->groups.size();
+    out->hits = context->mtile_hits;
+    out->misses = context->mtile_misses;
+    for (const auto& kv : context->mtile) out->resident_bytes += kv.second->bytes();
+    for (const auto& kv : context->groups) out->resident_bytes += kv.second->bytes();
+    return kOk;
+}
+
+int rocknpu_b200_status_code(int device_status) {
+    if (device_status == rk::kErrNone) return kOk;
+    return device_status == rk::kErrNonFinite ? kInvalid : kExecError;
+}
+
 int rocknpu_b200_context_check(rocknpu_context* context) {
     if (!context) return kInvalid;
     if (!bind(context)) return kDeviceError;

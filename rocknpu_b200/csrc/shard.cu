@@ -47,6 +47,10 @@ constexpr int kMaxRanks = ROCKNPU_B200_MAX_RANKS;
 constexpr size_t kSignalBytes = 4096;  // flags[kMaxRanks] at 0, epoch at 512
 constexpr size_t kEpochOffset = 512;
 
+// Wait limit of the peer barrier's flag spin (process-wide; the library's
+// 2 s default unless rocknpu_b200_set_peer_wait_limit_ms changed it).
+std::atomic<unsigned long long> g_peer_wait_limit_ns{rk::kWaitLimitNs};
+
 struct PeerPtrs {
     unsigned* sig[kMaxRanks];  // every rank's signal area, mapped here
 };
@@ -55,9 +59,10 @@ struct PeerPtrs {
 // publishes this rank's new epoch in rank t's flag slot `rank` and waits until
 // rank t's epoch has arrived in this rank's slot `t`.  The fence before the
 // release store orders every earlier write of this GPU (the preceding
-// kernels' peer stores included) before the flag.  Waits are bounded; on
-// timeout the kernel records kErrTimeoutPeer and returns.
-__global__ void peer_barrier_kernel(PeerPtrs peers, unsigned* local_sig, int rank, int world, int* err) {
+// kernels' peer stores included) before the flag.  Waits are bounded by
+// limit_ns; on timeout the kernel records kErrTimeoutPeer and returns.
+__global__ void peer_barrier_kernel(PeerPtrs peers, unsigned* local_sig, int rank, int world, int* err,
+                                    unsigned long long limit_ns) {
     __shared__ unsigned epoch;
     volatile unsigned* ep = local_sig + kEpochOffset / sizeof(unsigned);
     if (threadIdx.x == 0) epoch = *ep + 1u;
@@ -74,7 +79,7 @@ __global__ void peer_barrier_kernel(PeerPtrs peers, unsigned* local_sig, int ran
             unsigned v;
             asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
             if (static_cast<int>(v - e) >= 0) break;
-            if (rk::globaltimer_ns() - t0 > rk::kWaitLimitNs) {
+            if (rk::globaltimer_ns() - t0 > limit_ns) {
                 atomicCAS(err, 0, rk::kErrTimeoutPeer);
                 break;
             }
@@ -465,6 +470,13 @@ void* rocknpu_b200_peer_buffer_ptr(rocknpu_b200_peer_buffer* b, int r) {
     return b->mapped[r] + kSignalBytes;
 }
 
+int rocknpu_b200_set_peer_wait_limit_ms(uint32_t ms) {
+    if (ms > 600000u) return ROCKNPU_STATUS_INVALID_ARGUMENT;
+    g_peer_wait_limit_ns.store(ms == 0 ? rk::kWaitLimitNs : static_cast<unsigned long long>(ms) * 1000000ull,
+                               std::memory_order_relaxed);
+    return ROCKNPU_STATUS_OK;
+}
+
 int rocknpu_b200_peer_barrier(rocknpu_b200_peer_buffer* b, int* status, rocknpu_stream stream) {
     if (!b || !status) return ROCKNPU_STATUS_INVALID_ARGUMENT;
     PeerPtrs pp{};
@@ -473,7 +485,8 @@ int rocknpu_b200_peer_barrier(rocknpu_b200_peer_buffer* b, int* status, rocknpu_
         pp.sig[r] = reinterpret_cast<unsigned*>(b->mapped[r]);
     }
     peer_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
-        pp, reinterpret_cast<unsigned*>(b->local), b->rank, b->world, status);
+        pp, reinterpret_cast<unsigned*>(b->local), b->rank, b->world, status,
+        g_peer_wait_limit_ns.load(std::memory_order_relaxed));
     return cudaGetLastError() == cudaSuccess ? ROCKNPU_STATUS_OK : ROCKNPU_STATUS_EXECUTION_ERROR;
 }
 

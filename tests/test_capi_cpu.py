@@ -199,3 +199,15 @@ def test_supports_op_without_native_routes(clean_env):
     assert sup(Q4, 2048, 2048, 16)  # generic rule: m % 4, k % 256, n % 16
     assert not sup(Q4, 2048, 2048, 8)  # small M needs the native W8 path
     assert not sup(Q4, 2048, 9000, 16)  # n > 8192
+
+
+def test_status_code_mapping():
+    """Device status words map to the reference's status codes the way the
+    host-pointer entry points report them (rocknpu.h:27-32)."""
+    L = rk.lib()
+    assert L.rocknpu_b200_status_code(0) == rk.STATUS_OK
+    assert L.rocknpu_b200_status_code(1) == rk.STATUS_INVALID_ARGUMENT
+    for code in range(2, 8):
+        assert L.rocknpu_b200_status_code(code) == rk.STATUS_EXECUTION_ERROR
+    assert L.rocknpu_b200_set_peer_wait_limit_ms(600001) == rk.STATUS_INVALID_ARGUMENT
+    assert L.rocknpu_b200_set_peer_wait_limit_ms(0) == rk.STATUS_OK
