@@ -931,6 +931,38 @@ def cfg5_block(ms_list, steps, warmup, rank, world, route="peer", check=True):
     clocks = ClockSampler(torch.cuda.current_device())
     with clocks:
         clocks.mark("t_start")
+        # M = 1 decode GEMVs first (K5 on int8 rows, K5b on the Q4_K blocks),
+        # before the large GEMMs leave the GPU at its power cap
+        x1 = cfg5_activations(1)
+        gemv_ms = _timed(lambda: sm(x1), max(steps, 20), warmup, dist)
+        a8, a_s = sm.quantize(x1)
+        o1 = torch.empty(max(width, 1), dtype=torch.float32, device="cuda")
+        gemv_local = _timed(lambda: dev.gemv_w8a8(a8, a_s, sm.w8, sm.w_scales, out=o1), max(steps, 50), warmup,
+                            dist)
+        gbytes = width * CFG5_K + 8 * width + CFG5_K + 4
+        res["gemv_w8"] = {"kernel": "gemv_w8a8_kernel (int8 rows, dp4a)", "ms_per_step": round(gemv_ms, 4),
+                          "us_local": round(gemv_local * 1e3, 2),
+                          "gbs_local": round(gbytes / (gemv_local * 1e-3) / 1e9, 1),
+                          "hbm_frac": round(gbytes / (gemv_local * 1e-3) / 1e9 / hbm_peak, 4),
+                          "bytes": gbytes}
+        # the same M = 1 product straight from this rank's Q4_K blocks (K5b):
+        # 144 bytes per 256 weights instead of 256 + scales
+        if width:
+            layout = dev.kq_layout(4, torch.from_numpy(blocks).cuda(), CFG5_K, width)
+            xf = x1.reshape(-1).contiguous()
+            yq = torch.empty(width, dtype=torch.float32, device="cuda")
+            kq_status = dev.new_status()
+            kq_ms = _timed(lambda: dev.gemv_kq(4, layout, xf, width, kq_status, out=yq), max(steps, 50), warmup,
+                           dist)
+            torch.cuda.synchronize()
+            assert kq_status.item() == 0, "gemv_kq status error"
+            qbytes = layout.numel() + 4 * CFG5_K + 4 * width
+            res["gemv_q4k"] = {"kernel": "gemv_kq_kernel<Q4_K> (K-quant blocks, codes and scales applied in registers, dp2a)",
+                               "us_local": round(kq_ms * 1e3, 2),
+                               "gbs_local": round(qbytes / (kq_ms * 1e-3) / 1e9, 1),
+                               "hbm_frac": round(qbytes / (kq_ms * 1e-3) / 1e9 / hbm_peak, 4),
+                               "bytes": qbytes, "vs_gemv_w8": round(gemv_local / kq_ms, 3)}
+            del layout, yq
         for m in ms_list:
             x = cfg5_activations(m)
             ms = _timed(lambda: sm(x), steps, warmup, dist)
@@ -958,19 +990,6 @@ def cfg5_block(ms_list, steps, warmup, rank, world, route="peer", check=True):
                           "job_vs_floor": round(max(recv_ms, gemm_ms) / ms, 4)})
             res["gemm"][str(m)] = r
             del x, a8, a_s, local
-        # M = 1 decode GEMV (K5) over the same rows
-        x1 = cfg5_activations(1)
-        gemv_ms = _timed(lambda: sm(x1), max(steps, 20), warmup, dist)
-        a8, a_s = sm.quantize(x1)
-        o1 = torch.empty(max(width, 1), dtype=torch.float32, device="cuda")
-        gemv_local = _timed(lambda: dev.gemv_w8a8(a8, a_s, sm.w8, sm.w_scales, out=o1), max(steps, 50), warmup,
-                            dist)
-        gbytes = width * CFG5_K + 8 * width + CFG5_K + 4
-        res["gemv_w8"] = {"kernel": "gemv_w8a8_kernel (int8 rows, dp4a)", "ms_per_step": round(gemv_ms, 4),
-                          "us_local": round(gemv_local * 1e3, 2),
-                          "gbs_local": round(gbytes / (gemv_local * 1e-3) / 1e9, 1),
-                          "hbm_frac": round(gbytes / (gemv_local * 1e-3) / 1e9 / hbm_peak, 4),
-                          "bytes": gbytes}
         clocks.mark("t_end")
     sm.check()
     if world > 1 and check:

@@ -207,6 +207,30 @@ int rocknpu_b200_gemm_f16(const uint16_t *a_f16, size_t ld_a, const uint16_t *w_
 int rocknpu_b200_gemv_w8a8(const int8_t *a_i8, const float *a_scale, const int8_t *w_i8, const float *w_scales,
                            float *out, size_t k, size_t n, rocknpu_stream stream);
 
+/* K5b: the decode GEMV that reads K-quant blocks directly (Q4_K: kind 4,
+ * Q6_K: kind 6; k % 256 == 0): y[n] = sum_k W[n][k] * x[k] with the weights'
+ * codes and sub-block scales applied in registers, no tensor cores and no
+ * int8 copy of the weight -- a decode step moves 0.5625 (Q4_K) or 0.8203
+ * (Q6_K) bytes per weight, the property for which the reference keeps M=1
+ * on llama.cpp's K-quant kernels by default (ggml-rocknpu.cpp:305-312).
+ * Numerics: each weight is ggml's f32 dequantisation, x is held as 16-bit
+ * fixed point per block of 32 values (scale = block max / 32767), the code
+ * products are exact int32 sums; outputs are within 1e-3 relative (and about
+ * 1e-6 of sum |w x|) of the exact dot product of the f32 weights, not
+ * bit-identical to a particular summation order.  A non-finite x sets
+ * *status to 1 and leaves y unspecified.  `layout` is the weight's decode
+ * layout (16-byte aligned, rocknpu_b200_kq_layout); x is 16-byte aligned;
+ * k up to 24576 (longer rows return ROCKNPU_STATUS_INVALID_ARGUMENT). */
+size_t rocknpu_b200_kq_layout_bytes(uint32_t kind, size_t k, size_t n);
+/* Write the decode layout of n rows of ggml blocks (device pointers): Q4_K
+ * the blocks unchanged; Q6_K the 208-byte block bodies (ql, qh, scales) of
+ * every row, then the f16 d of every block -- the same 210 bytes per block,
+ * arranged so that every block is 16-byte aligned. */
+int rocknpu_b200_kq_layout(uint32_t kind, const uint8_t *blocks, size_t k, size_t n, uint8_t *layout,
+                           rocknpu_stream stream);
+int rocknpu_b200_gemv_kq(uint32_t kind, const uint8_t *layout, size_t k, size_t n, const float *x, float *y,
+                         int *status, rocknpu_stream stream);
+
 /* ---- 3. multi-GPU N-sharding (one process per GPU, one node) ----------- */
 
 #define ROCKNPU_B200_MAX_RANKS 16

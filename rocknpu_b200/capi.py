@@ -76,6 +76,9 @@ SIGNATURES = {
     "rocknpu_b200_convert_f16": (_I, [_P, _S, _S, _S, _P, _S, _P]),
     "rocknpu_b200_gemm_f16": (_I, [_P, _S, _P, _S, _P, _S, _S, _S, _S, _P, _P]),
     "rocknpu_b200_gemv_w8a8": (_I, [_P, _P, _P, _P, _P, _S, _S, _P]),
+    "rocknpu_b200_kq_layout_bytes": (_S, [_U32, _S, _S]),
+    "rocknpu_b200_kq_layout": (_I, [_U32, _P, _S, _S, _P, _P]),
+    "rocknpu_b200_gemv_kq": (_I, [_U32, _P, _S, _S, _P, _P, _P, _P]),
     "rocknpu_b200_shard_rows": (_S, [_S, _S, _P, _P]),
     "rocknpu_b200_gather_shards": (_I, [_P, _S, _S, _S, _S, _P, _P, _P, _S, _P]),
     "rocknpu_b200_peer_buffer_create": (_I, [_S, _I, _I, _P, _P]),

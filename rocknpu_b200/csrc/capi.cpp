@@ -1478,4 +1478,32 @@ int rocknpu_b200_gemv_w8a8(const int8_t* a_i8, const float* a_scale, const int8_
     return cuda_status(cudaGetLastError());
 }
 
+size_t rocknpu_b200_kq_layout_bytes(uint32_t kind, size_t k, size_t n) {
+    if ((kind != 4 && kind != 6) || k == 0 || k % 256 != 0) return 0;
+    return rk::kq_layout_bytes(static_cast<int>(kind), k, n);
+}
+
+int rocknpu_b200_kq_layout(uint32_t kind, const uint8_t* blocks, size_t k, size_t n, uint8_t* layout,
+                           rocknpu_stream stream) {
+    if ((kind != 4 && kind != 6) || !blocks || !layout || k == 0 || n == 0 || k % 256 != 0 || k > 0x7fffffff ||
+        n > 0x7fffffff)
+        return kInvalid;
+    if (kind == 6 && (reinterpret_cast<uintptr_t>(blocks) % 2 || reinterpret_cast<uintptr_t>(layout) % 16))
+        return kInvalid;
+    return cuda_status(static_cast<cudaError_t>(rk::launch_kq_layout(static_cast<int>(kind), blocks,
+                                                                     static_cast<int>(k), static_cast<int>(n), layout,
+                                                                     static_cast<cudaStream_t>(stream))));
+}
+
+int rocknpu_b200_gemv_kq(uint32_t kind, const uint8_t* layout, size_t k, size_t n, const float* x, float* y,
+                         int* status, rocknpu_stream stream) {
+    if ((kind != 4 && kind != 6) || !layout || !x || !y || !status || k == 0 || n == 0 || k % 256 != 0 ||
+        k > 0x7fffffff || n > 0x7fffffff)
+        return kInvalid;
+    const int e = rk::launch_gemv_kq(static_cast<int>(kind), layout, static_cast<int>(k), static_cast<int>(n), x, y,
+                                     status, static_cast<cudaStream_t>(stream));
+    if (e == cudaErrorInvalidValue) return kInvalid;
+    return cuda_status(static_cast<cudaError_t>(e));
+}
+
 }  // extern "C"

@@ -104,6 +104,26 @@ def gemv_w8a8(a8: torch.Tensor, a_scale: torch.Tensor, w8: torch.Tensor, w_scale
     return out
 
 
+def kq_layout(kind: int, blocks: torch.Tensor, k: int, n: int, stream=None) -> torch.Tensor:
+    """Decode layout of a K-quant weight (device uint8 blocks, n rows of k)."""
+    nbytes = int(lib().rocknpu_b200_kq_layout_bytes(kind, k, n))
+    if nbytes == 0:
+        raise ValueError(f"no decode layout for kind {kind}, k={k}")
+    out = torch.empty(nbytes, dtype=torch.uint8, device=blocks.device)
+    _check(lib().rocknpu_b200_kq_layout(kind, blocks.data_ptr(), k, n, out.data_ptr(), _stream(stream)), "kq_layout")
+    return out
+
+
+def gemv_kq(kind: int, layout: torch.Tensor, x: torch.Tensor, n: int, status: torch.Tensor,
+            out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """K5b: y[n] = dequant(W) . x straight from the K-quant decode layout."""
+    k = x.numel()
+    out = torch.empty(n, dtype=torch.float32, device=x.device) if out is None else out
+    _check(lib().rocknpu_b200_gemv_kq(kind, layout.data_ptr(), k, n, x.data_ptr(), out.data_ptr(),
+                                      status.data_ptr(), _stream(stream)), "gemv_kq")
+    return out
+
+
 def matmul_w8a8(ctx, a: torch.Tensor, w8: torch.Tensor, w_scales: torch.Tensor, out: torch.Tensor, stream=None):
     """K2 + K3 (K5 at m == 1) through a context's workspace."""
     m, k = a.shape
