@@ -100,6 +100,29 @@ def layer_plan(layer: int):
             ("down", [(down_kind, HIDDEN)], FFN)]
 
 
+def planned_layer_calls(m: int):
+    """The plugin's own decisions for this model's layers in steady state
+    (rocknpu_graph_plan over the splits llama.cpp hands the plugin), in the
+    form of layer_plan(): [(call, [(kind, n)], k)] per layer.  Our arm checks
+    that layer_plan() -- which the reference arm replays without loading the
+    library -- is exactly this list."""
+    from rocknpu_b200 import plugin
+    spec = {"hidden": HIDDEN, "ffn": FFN, "kv": KV}
+    out = []
+    for calls in plugin.layer_calls(spec, m, LAYERS):
+        out.append([(c, [(plugin.TYPE_TO_KIND[t], n) for (_, t, n) in members], k) for c, members, k in calls])
+    return out
+
+
+def check_layer_plan(m: int) -> str:
+    planned = planned_layer_calls(m)
+    for layer in range(LAYERS):
+        want = [("concat" if len(members) > 1 else "single", members, k) for _, members, k in layer_plan(layer)]
+        if planned[layer] != want:
+            raise RuntimeError(f"layer {layer}: the plugin plans {planned[layer]}, the bench replays {want}")
+    return "rocknpu_graph_plan (the plugin's graph_compute decisions, steady state)"
+
+
 def algorithmic(m: int):
     """Bytes and int8 ops of the GEMM launches of one step (K3 only): int8
     weights + int8 activations + f32 output + scales, and 2*m*n*k."""
@@ -330,6 +353,7 @@ def run_ours(args, rank: int, world: int):
     int8_peak_tops = 2.0 * bf16_peak  # dense int8 = 2x dense bf16 on B200
 
     t0 = time.time()
+    plan_source = check_layer_plan(m)
     weights = make_weights()
     acts = make_activations(m, seed=5000 + 97 * rank)
     gen_s = time.time() - t0
@@ -583,6 +607,7 @@ def run_ours(args, rank: int, world: int):
         "cpu_baseline": cpu,
         "gpu_launches": launches_per_step * args.steps if launches_per_step is not None else None,
         "launches_per_step": launches_per_step,
+        "calls_planned_by": plan_source,
         "clocks": clocks.summary(),
         "setup_s": round(gen_s, 1),
     }

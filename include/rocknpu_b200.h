@@ -69,6 +69,76 @@ void rocknpu_apply_default_env(void);
  * switches included. */
 int rocknpu_mul_mat_supported(const rocknpu_mul_mat_desc *desc);
 
+/* The plugin's graph_compute dispatch (rocknpu_backend_graph_compute,
+ * ggml-rocknpu.cpp:978-1650, with rocknpu_mtile_group :838-976) as a planner:
+ * given the nodes of one ggml graph split it returns, in order, the C-ABI
+ * calls the plugin makes for them, without making them.  What the plugin
+ * carries from split to split and from one graph evaluation to the next --
+ * the per-layer QKV stash of prompt batches (:32-53, :506-516, :868-928), the
+ * decode triple's weight references and stability count (:1185-1258), the
+ * pending FFN composite (:1300-1318) -- lives in a rocknpu_graph_state.
+ * Decisions assume every call succeeds (the plugin falls back to the
+ * per-node path when a group call fails).  The hybrid CPU/NPU split of
+ * ROCKNPU_DECODE=hybrid (:400-489) needs ggml's CPU backend and is not
+ * planned: with it set, planned calls are the NPU-only forms. */
+enum rocknpu_graph_op {
+    ROCKNPU_OP_MUL_MAT = 1,
+    ROCKNPU_OP_VIEW = 2,  /* GGML_OP_NONE, RESHAPE, VIEW, PERMUTE, TRANSPOSE: nothing to run */
+    ROCKNPU_OP_OTHER = 3, /* anything else: graph_compute fails */
+};
+
+typedef struct rocknpu_graph_node {
+    int32_t op;                  /* rocknpu_graph_op */
+    int32_t compute;             /* GGML_TENSOR_FLAG_COMPUTE is set */
+    rocknpu_mul_mat_desc desc;   /* MUL_MAT: src0, src1 and dst as supports_op reads them */
+    const char *weight_name;     /* src0->name, e.g. "blk.3.attn_q.weight" */
+    const void *weight;          /* src0->data: the weight's identity (the caches key on it) */
+    size_t weight_bytes;         /* ggml_nbytes(src0) */
+    const void *activation;      /* src1: the activation tensor's identity */
+    const void *activation_data; /* src1->data */
+    int32_t has_w8;              /* a W8 sidecar exists for the weight (rocknpu_w8_sidecar_get succeeds) */
+} rocknpu_graph_node;
+
+enum rocknpu_graph_call {
+    ROCKNPU_CALL_CONCAT = 1,            /* rocknpu_matmul_q_concat_f32_f32_mtile over the members */
+    ROCKNPU_CALL_STASH = 2,             /* the node's output copied from its layer's QKV stash */
+    ROCKNPU_CALL_RELEASE = 3,           /* rocknpu_mtile_release of the members' weights */
+    ROCKNPU_CALL_OUTPUT_HEAD_NSPLIT = 4,/* rocknpu_matmul_w8a8_f32_f32_m1_nsplit, chunks of 8192 */
+    ROCKNPU_CALL_FFN_DEFER = 5,         /* M=1 gate/up kept for the down node (ROCKNPU_FFN_COMPOSITE) */
+    ROCKNPU_CALL_SWIGLU_DOWN = 6,       /* rocknpu_matmul_w8a8_swiglu_down_f32 */
+    ROCKNPU_CALL_TRIPLE_M1 = 7,         /* q/v/k: rocknpu_matmul_w8a8_triple_f32_f32_m1 (w8) or _q_triple_ */
+    ROCKNPU_CALL_PAIR_M1 = 8,           /* gate/up or v/k: rocknpu_matmul_w8a8_pair_f32_f32_m1 (w8) or _q_pair_ */
+    ROCKNPU_CALL_PAIR_MTILE = 9,        /* rocknpu_matmul_q_pair_f32_f32_mtile */
+    ROCKNPU_CALL_CHUNKED_M16 = 10,      /* m / 16 single calls of 16 rows each */
+    ROCKNPU_CALL_SINGLE = 11,           /* rocknpu_matmul_{q4_k,q5_k,q6_k,f16}_f32_f32, or w8a8_f32_f32_m1 (w8) */
+    ROCKNPU_CALL_PREWARM = 12,          /* rocknpu_prewarm_quantized_m16 before a CPU fallback */
+    ROCKNPU_CALL_CPU_FALLBACK = 13,     /* the whole split to the CPU backend (ROCKNPU_RUNTIME_M16_ROUTER) */
+    ROCKNPU_CALL_FAILED = 14,           /* graph_compute returns GGML_STATUS_FAILED at `node` */
+};
+
+typedef struct rocknpu_graph_action {
+    int32_t call;            /* rocknpu_graph_call */
+    int32_t node;            /* the node being dispatched */
+    int32_t count;           /* members (1..4) */
+    int32_t members[4];      /* node index per member; -1 for a weight held by the layer state */
+    const void *weights[4];  /* each member's weight identity */
+    int32_t w8;              /* the call's native W8 (sidecar) form */
+    int32_t layer;           /* blk.<layer> of a QKV stash or triple decision, -1 otherwise */
+    int64_t m, k, n;         /* rows, depth, total output columns of the call */
+} rocknpu_graph_action;
+
+typedef struct rocknpu_graph_state rocknpu_graph_state;
+/* cpu_fallback: the backend was created with ROCKNPU_RUNTIME_M16_ROUTER set
+ * (rocknpu_device_init, ggml-rocknpu.cpp:1687-1703).  NULL on failure. */
+rocknpu_graph_state *rocknpu_graph_state_create(int32_t cpu_fallback);
+void rocknpu_graph_state_destroy(rocknpu_graph_state *state);
+/* Plan one split: writes the calls, in order, into actions[0..capacity) and
+ * returns their number; -1 for a NULL argument or too small a capacity
+ * (4 * count + 4 always suffices).  Environment switches are read on each
+ * call, as the plugin reads them. */
+int rocknpu_graph_plan(rocknpu_graph_state *state, const rocknpu_graph_node *nodes, size_t count,
+                       rocknpu_graph_action *actions, size_t capacity);
+
 /* ---- 2. device-pointer entry points ------------------------------------ */
 
 /* Opaque CUDA stream (cudaStream_t). */

@@ -60,6 +60,9 @@ SIGNATURES = {
     # rocknpu_b200.h
     "rocknpu_apply_default_env": (None, []),
     "rocknpu_mul_mat_supported": (_I, [_P]),
+    "rocknpu_graph_state_create": (_P, [ctypes.c_int32]),
+    "rocknpu_graph_state_destroy": (None, [_P]),
+    "rocknpu_graph_plan": (_I, [_P, _P, _S, _P, _S]),
     "rocknpu_b200_context_stream": (_P, [_P]),
     "rocknpu_b200_context_check": (_I, [_P]),
     "rocknpu_b200_status_code": (_I, [_I]),
