@@ -109,11 +109,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const CUtensorMap* map = is_w ? &p.tmap_w : &p.tmap_a;
             const uint32_t box = is_w ? C::kWBox : C::kABox;
             const int off = is_w ? 0 : C::kWBox;
+            // first unit's coordinates before the dependency wait
+            Unit t = unit_coords<256, BT>(p, pair);
             if (!is_w) griddep_wait();
             int g = 0;
             bool ok = true;
             for (int u = pair; ok && u < p.units; u += npairs) {
-                const Unit t = unit_coords<256, BT>(p, u);
+                if (u != pair) t = unit_coords<256, BT>(p, u);
                 const int row =
                     is_w ? t.n0 + 128 * static_cast<int>(rank) : t.m0 + (BT / 2) * static_cast<int>(rank);
                 for (int kb = t.kb0; kb < t.kb1; ++kb, ++g) {
