@@ -982,7 +982,7 @@ def cfg5_block(ms_list, steps, warmup, rank, world, route="peer", check=True):
             torch.cuda.synchronize()
             assert kq_status.item() == 0, "gemv_kq status error"
             qbytes = layout.numel() + 4 * CFG5_K + 4 * width
-            res["gemv_q4k"] = {"kernel": "gemv_kq_kernel<Q4_K> (K-quant blocks, codes and scales applied in registers, dp2a)",
+            res["gemv_q4k"] = {"kernel": "gemv_q4k_kernel (Q4_K code and header planes in bulk-copied row stages, codes and scales applied in registers, dp2a)",
                                "us_local": round(kq_ms * 1e3, 2),
                                "gbs_local": round(qbytes / (kq_ms * 1e-3) / 1e9, 1),
                                "hbm_frac": round(qbytes / (kq_ms * 1e-3) / 1e9 / hbm_peak, 4),

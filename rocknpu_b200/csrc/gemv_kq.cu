@@ -1,49 +1,41 @@
 // K5b: M=1 decode GEMV straight from K-quant superblocks, y[n] = W[n, k] . x[k]
-// with W dequantised to f32 in registers (no tensor cores, no int8 copy).
+// with W dequantised in registers (no tensor cores, no int8 copy): the Q6_K
+// kernel and the layout / launch entry points for both kinds (the Q4_K
+// kernel is in gemv_q4k.cu).
 //
 // Why: a decode step streams every weight once, so its time is the weight
-// bytes over HBM bandwidth.  Q4_K is 0.5625 bytes per weight, the prepared
-// int8 rows of the W8A8 path 1 + 4/k -- the reference keeps M=1 on
-// llama.cpp's Q4_K kernels for exactly that reason (ggml-rocknpu.cpp:305-312).
-// This kernel reads the Q4_K / Q6_K blocks themselves.
+// bytes over HBM bandwidth.  Q4_K is 0.5625 bytes per weight, Q6_K 0.8203,
+// the prepared int8 rows of the W8A8 path 1 + 4/k -- the reference keeps
+// M=1 on llama.cpp's K-quant kernels for exactly that reason
+// (ggml-rocknpu.cpp:305-312).
 //
-// Numerics: every weight is ggml's f32 dequantisation (Q4_K: d * sc * q -
-// dmin * m over 32-weight sub-blocks; Q6_K: d * sc * (q - 32) over 16-weight
-// sub-blocks), applied per sub-block rather than per weight:
-//   sum_i w_i x_i = A * sum_i q_i x_i - B * sum_i x_i.
-// x is held as 16-bit fixed point per block of 32 (X = rint(x * 32767 /
-// max|x|), x ~ X * s), so sum_i q_i X_i is an exact int32 dp2a sum (two
-// code-times-X products per instruction, codes unpacked with one mask per 4).
-// Representing x that way moves each x by at most 1/65534 of its block's
-// largest magnitude; the outputs land within ~1e-6 of sum |w x| of the exact
-// dot product of the f32 weights (the tests assert the north_star's 1e-3
-// relative bound with that cancellation term).
+// Numerics: every weight is ggml's f32 dequantisation (Q6_K: d * sc * (q -
+// 32) over 16-weight sub-blocks), applied per sub-block rather than per
+// weight: sum_i w_i x_i = d sc (sum_i q_i x_i - 32 sum_i x_i).  x is held as
+// 16-bit fixed point per block of 32 (X = rint(x * 32767 / max|x|), x ~ X *
+// s), so sum_i q_i X_i is an exact int32 dp2a sum.  Representing x that way
+// moves each x by at most 1/65534 of its block's largest magnitude; the
+// outputs land within ~1e-6 of sum |w x| of the exact dot product of the f32
+// weights (the tests assert the north_star's 1e-3 relative bound with that
+// cancellation term).
 //
-// Layout in HBM ("decode layout", prepared once per resident weight):
-//   Q4_K  the ggml blocks unchanged: 144 bytes = 9 x 16, so every block and
-//         row is 16-byte aligned;
-//   Q6_K  each 210-byte block without its trailing f16 d: 208 bytes = 13 x 16
-//         (ql[128], qh[64], scales[16]), rows of 208 * k/256 bytes, followed by
-//         the d values [n][k/256] as f16 -- the same 210 bytes per block, laid
-//         out so that 128-bit loads and bulk copies stay aligned.
+// Q6_K decode layout: each 210-byte block without its trailing f16 d: 208
+// bytes = 13 x 16 (ql[128], qh[64], scales[16]), rows of 208 * k/256 bytes,
+// followed by the d values [n][k/256] as f16 -- the same 210 bytes per
+// block, laid out so that 128-bit copies stay aligned.
 //
 // Kernel: persistent CTAs of 8 warps (two per SM).  Each warp walks its own
 // sequence of row sets (32 / seg consecutive rows, seg = the power of two at
 // or above k / 256, at most 32) and streams them into its own shared-memory
 // ring with 16-byte cp.async copies issued by all 32 lanes -- coalesced, 512
 // bytes per instruction, one set ahead.  A lane then takes whole
-// superblocks (256 weights) of one row from shared memory, so a block's
-// header -- d, dmin and the 8 packed scale/min pairs, or Q6_K's 16 scales --
-// is decoded once per 256 weights, and the row's partial sums are reduced
-// with shuffles inside its segment of seg lanes.  No block-wide barrier after
-// the prologue and no spin: a warp waits only for its own copies.  x is
-// quantised once per CTA into shared memory as int16 with 16 bytes of padding
-// per 256 values, so lanes on neighbouring blocks read different banks.
-// Shared-memory reads (x and the codes) bound it: ~0.5 of HBM bandwidth on
-// the 132 MB cfg5 weight.  (Measured on B200 and not kept: a single producer
-// thread moving 8-row stages with cp.async.bulk, 4 rows sharing each x read,
-// 0.58 -- 0.8 with the arithmetic removed; per-lane loads of whole 144-byte
-// blocks straight into registers, 0.4: 32 scattered sectors per instruction.)
+// superblocks (256 weights) of one row from shared memory, so a block's 16
+// scales are read once per 256 weights, and the row's partial sums are
+// reduced with shuffles inside its segment of seg lanes.  No block-wide
+// barrier after the prologue and no spin: a warp waits only for its own
+// copies.  x is quantised once per CTA into shared memory as int16 with 16
+// bytes of padding per 256 values, so lanes on neighbouring blocks read
+// different banks.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -96,60 +88,6 @@ __device__ __forceinline__ float byte_f(uint32_t v) {
 template <int J>
 __device__ __forceinline__ float sbyte_f(uint32_t v) {
     return static_cast<float>(static_cast<int8_t>((v >> (8 * J)) & 0xFFu));
-}
-
-// One Q4_K superblock of one row: sum over its 256 weights of w * x (x as
-// held).  xb: the block's x values (int16, contiguous); xs: its 8 sub-block
-// x scales; xm: their sums of x as held.  ggml's 6-bit packing of the scale
-// bytes s[0..11] is unpacked four sub-blocks per register: j < 4 takes
-// s[j] & 63 (scale) and s[j+4] & 63 (min); j >= 4 the low (scale) or high
-// (min) nibble of s[j+4] under the top two bits of s[j-4] (scale) or s[j]
-// (min).  High-nibble codes are used in place (code * 16, the 1/16 folded
-// into the scale).
-__device__ __forceinline__ float q4k_block(const uint4* __restrict__ blk, const uint8_t* __restrict__ xb,
-                                           const float* __restrict__ xs, const float* __restrict__ xm) {
-    int sq[8];
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {  // quarter g: sub-blocks 2g (low nibbles) and 2g+1 (high)
-        const uint4 qa = blk[1 + 2 * g];
-        const uint4 qb = blk[2 + 2 * g];
-        const uint4* xp = reinterpret_cast<const uint4*>(xb + 128 * g);
-        const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-        int lo0 = 0, lo1 = 0, hi0 = 0, hi1 = 0;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {  // 8 positions: words 2c, 2c+1
-            const uint4 xl = xp[c], xh = xp[4 + c];
-            lo0 = dot4(w[2 * c] & 0x0F0F0F0Fu, xl.x, xl.y, lo0);
-            lo1 = dot4(w[2 * c + 1] & 0x0F0F0F0Fu, xl.z, xl.w, lo1);
-            hi0 = dot4(w[2 * c] & 0xF0F0F0F0u, xh.x, xh.y, hi0);
-            hi1 = dot4(w[2 * c + 1] & 0xF0F0F0F0u, xh.z, xh.w, hi1);
-        }
-        sq[2 * g] = lo0 + lo1;
-        sq[2 * g + 1] = hi0 + hi1;
-    }
-    const uint4 hdr = blk[0];
-    const uint32_t sc_lo = hdr.y & 0x3F3F3F3Fu, m_lo = hdr.z & 0x3F3F3F3Fu;
-    const uint32_t sc_hi = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
-    const uint32_t m_hi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
-    // sum_i (d sc_j q_i - dmin m_j) x_i = d * sum_j sc_j s_j (sum q X)_j - dmin * sum_j m_j (sum x)_j
-    float qx = byte_f<0>(sc_lo) * (xs[0] * static_cast<float>(sq[0]));
-    qx = fmaf(byte_f<1>(sc_lo), (0.0625f * xs[1]) * static_cast<float>(sq[1]), qx);
-    qx = fmaf(byte_f<2>(sc_lo), xs[2] * static_cast<float>(sq[2]), qx);
-    qx = fmaf(byte_f<3>(sc_lo), (0.0625f * xs[3]) * static_cast<float>(sq[3]), qx);
-    qx = fmaf(byte_f<0>(sc_hi), xs[4] * static_cast<float>(sq[4]), qx);
-    qx = fmaf(byte_f<1>(sc_hi), (0.0625f * xs[5]) * static_cast<float>(sq[5]), qx);
-    qx = fmaf(byte_f<2>(sc_hi), xs[6] * static_cast<float>(sq[6]), qx);
-    qx = fmaf(byte_f<3>(sc_hi), (0.0625f * xs[7]) * static_cast<float>(sq[7]), qx);
-    float mx = byte_f<0>(m_lo) * xm[0];
-    mx = fmaf(byte_f<1>(m_lo), xm[1], mx);
-    mx = fmaf(byte_f<2>(m_lo), xm[2], mx);
-    mx = fmaf(byte_f<3>(m_lo), xm[3], mx);
-    mx = fmaf(byte_f<0>(m_hi), xm[4], mx);
-    mx = fmaf(byte_f<1>(m_hi), xm[5], mx);
-    mx = fmaf(byte_f<2>(m_hi), xm[6], mx);
-    mx = fmaf(byte_f<3>(m_hi), xm[7], mx);
-    const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&hdr.x));
-    return fmaf(dm.x, qx, -dm.y * mx);
 }
 
 // One Q6_K superblock (decode layout: ql[128], qh[64], scales[16]) of one
@@ -213,7 +151,7 @@ constexpr int kSlots = 2;
 
 // Shared memory: [warps][kSlots][slot_bytes] row-set ring | x as int16,
 // padded | x scale per 32 | sum of X per 16 | sum of x as held per 32.
-template <int KIND, int SLOTS>
+template <int SLOTS>
 __global__ void __launch_bounds__(kKqThreads, 2) gemv_kq_kernel(const KqParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -221,7 +159,6 @@ __global__ void __launch_bounds__(kKqThreads, 2) gemv_kq_kernel(const KqParams p
     uint8_t* xq = smem + static_cast<size_t>(kKqWarps) * SLOTS * p.slot_bytes;
     float* xscale = reinterpret_cast<float*>(xq + xq_off(p.k));
     int* xsum16 = reinterpret_cast<int*>(xscale + p.k / 32);
-    float* xmean32 = reinterpret_cast<float*>(xsum16 + p.k / 16);  // scale * sum X per 32
 
     // This warp's row sets: first, first + stride, ...  A set is the
     // rows_per_warp consecutive rows the warp works on at once.
@@ -279,7 +216,6 @@ __global__ void __launch_bounds__(kKqThreads, 2) gemv_kq_kernel(const KqParams p
         xsum16[2 * blk + 1] = s1;
         const float scale = (finite && m > 0.f) ? m / 32767.f : 0.f;
         xscale[blk] = scale;
-        xmean32[blk] = scale * static_cast<float>(s0 + s1);
     }
     __syncthreads();
 
@@ -299,13 +235,9 @@ __global__ void __launch_bounds__(kKqThreads, 2) gemv_kq_kernel(const KqParams p
             const uint8_t* rowp = ring + static_cast<size_t>(it % SLOTS) * p.slot_bytes + static_cast<size_t>(rw) * p.row_bytes;
             for (int b = b0; b < p.nb; b += p.seg) {
                 const uint8_t* xb = xq + xq_off(256 * b);
-                if constexpr (KIND == kQ4K) {
-                    acc += q4k_block(reinterpret_cast<const uint4*>(rowp + 144 * b), xb, xscale + 8 * b, xmean32 + 8 * b);
-                } else {
-                    const float dv = __half2float(p.d6[static_cast<size_t>(row) * p.nb + b]);
-                    acc += q6k_block(reinterpret_cast<const uint4*>(rowp + kQ6Body * b), dv, xb, xscale + 8 * b,
-                                     xsum16 + 16 * b);
-                }
+                const float dv = __half2float(p.d6[static_cast<size_t>(row) * p.nb + b]);
+                acc += q6k_block(reinterpret_cast<const uint4*>(rowp + kQ6Body * b), dv, xb, xscale + 8 * b,
+                                 xsum16 + 16 * b);
             }
         }
         for (int o = p.seg >> 1; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
@@ -341,8 +273,7 @@ size_t kq_layout_bytes(int kind, size_t k, size_t n) {
 
 int launch_kq_layout(int kind, const uint8_t* blocks, int k, int n, uint8_t* layout, cudaStream_t s) {
     const long long nb = k / 256;
-    if (kind == kQ4K)
-        return cudaMemcpyAsync(layout, blocks, static_cast<size_t>(n) * nb * 144, cudaMemcpyDeviceToDevice, s);
+    if (kind == kQ4K) return launch_q4k_layout(blocks, k, n, layout, s);
     if (kind != kQ6K) return cudaErrorInvalidValue;
     const long long nblocks = static_cast<long long>(n) * nb;
     const int grid = static_cast<int>(std::min<long long>((nblocks + 7) / 8, 148LL * 16));
@@ -357,7 +288,8 @@ int launch_kq_layout(int kind, const uint8_t* blocks, int k, int n, uint8_t* lay
 // Rows too long for one slot per warp in ~220 KB are rejected.
 int launch_gemv_kq(int kind, const uint8_t* layout, int k, int n, const float* x, float* y, int* err,
                    cudaStream_t s) {
-    if ((kind != kQ4K && kind != kQ6K) || k <= 0 || k % 256 != 0 || n <= 0 || !layout || !x || !y || !err)
+    if (kind == kQ4K) return launch_gemv_q4k(layout, k, n, x, y, err, s);
+    if (kind != kQ6K || k <= 0 || k % 256 != 0 || n <= 0 || !layout || !x || !y || !err)
         return cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(layout) % 16) || (reinterpret_cast<uintptr_t>(x) % 16))
         return cudaErrorInvalidValue;
@@ -365,17 +297,17 @@ int launch_gemv_kq(int kind, const uint8_t* layout, int k, int n, const float* x
     p.k = k;
     p.n = n;
     p.nb = k / 256;
-    p.row_bytes = p.nb * (kind == kQ4K ? 144 : kQ6Body);
+    p.row_bytes = p.nb * kQ6Body;
     p.seg = 1;
     while (p.seg < p.nb && p.seg < 32) p.seg <<= 1;
     p.rows_per_warp = 32 / p.seg;
     p.slot_bytes = p.rows_per_warp * p.row_bytes;
     p.w = layout;
-    p.d6 = kind == kQ6K ? reinterpret_cast<const __half*>(layout + static_cast<size_t>(n) * p.nb * kQ6Body) : nullptr;
+    p.d6 = reinterpret_cast<const __half*>(layout + static_cast<size_t>(n) * p.nb * kQ6Body);
     p.x = x;
     p.y = y;
     p.err = err;
-    const size_t xbytes = static_cast<size_t>(2 * k + 16 * (k / 256)) + 8 * static_cast<size_t>(k / 32) +
+    const size_t xbytes = static_cast<size_t>(2 * k + 16 * (k / 256)) + 4 * static_cast<size_t>(k / 32) +
                           4 * static_cast<size_t>(k / 16);
     constexpr size_t kBudget = 220u * 1024u;
     int slots = 0;
@@ -387,37 +319,29 @@ int launch_gemv_kq(int kind, const uint8_t* layout, int k, int n, const float* x
     }
     if (slots == 0) return cudaErrorInvalidValue;
     const size_t smem = static_cast<size_t>(kKqWarps) * slots * p.slot_bytes + xbytes;
-    // the shared-memory limit is raised once per device, kind and depth
-    static bool attr_done[64][2][4] = {};
+    // the shared-memory limit is raised once per device and depth
+    static bool attr_done[64][4] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    const int ki = kind == kQ4K ? 0 : 1;
-    const void* fn = nullptr;
-    if (kind == kQ4K)
-        fn = slots == 4   ? reinterpret_cast<const void*>(gemv_kq_kernel<kQ4K, 4>)
-             : slots == 3 ? reinterpret_cast<const void*>(gemv_kq_kernel<kQ4K, 3>)
-             : slots == 2 ? reinterpret_cast<const void*>(gemv_kq_kernel<kQ4K, 2>)
-                          : reinterpret_cast<const void*>(gemv_kq_kernel<kQ4K, 1>);
-    else
-        fn = slots == 4   ? reinterpret_cast<const void*>(gemv_kq_kernel<kQ6K, 4>)
-             : slots == 3 ? reinterpret_cast<const void*>(gemv_kq_kernel<kQ6K, 3>)
-             : slots == 2 ? reinterpret_cast<const void*>(gemv_kq_kernel<kQ6K, 2>)
-                          : reinterpret_cast<const void*>(gemv_kq_kernel<kQ6K, 1>);
-    if (!attr_done[dev][ki][slots - 1]) {
+    const void* fn = slots == 4   ? reinterpret_cast<const void*>(gemv_kq_kernel<4>)
+                     : slots == 3 ? reinterpret_cast<const void*>(gemv_kq_kernel<3>)
+                     : slots == 2 ? reinterpret_cast<const void*>(gemv_kq_kernel<2>)
+                                  : reinterpret_cast<const void*>(gemv_kq_kernel<1>);
+    if (!attr_done[dev][slots - 1]) {
         const cudaError_t e =
             cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kBudget));
         if (e != cudaSuccess) return e;
-        attr_done[dev][ki][slots - 1] = true;
+        attr_done[dev][slots - 1] = true;
     }
-    // CTAs per SM for this shared-memory size (cached per device, kind, depth)
-    static int occ[64][2][4] = {};
-    static size_t occ_smem[64][2][4] = {};
-    int& per_sm = occ[dev][ki][slots - 1];
-    if (per_sm == 0 || occ_smem[dev][ki][slots - 1] != smem) {
+    // CTAs per SM for this shared-memory size (cached per device and depth)
+    static int occ[64][4] = {};
+    static size_t occ_smem[64][4] = {};
+    int& per_sm = occ[dev][slots - 1];
+    if (per_sm == 0 || occ_smem[dev][slots - 1] != smem) {
         int b = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, fn, kKqThreads, smem) != cudaSuccess) b = 1;
         per_sm = std::max(b, 1);
-        occ_smem[dev][ki][slots - 1] = smem;
+        occ_smem[dev][slots - 1] = smem;
     }
     const int sets = (n + p.rows_per_warp - 1) / p.rows_per_warp;
     const int grid = std::max(1, std::min((sets + kKqWarps - 1) / kKqWarps, sm_count() * per_sm));

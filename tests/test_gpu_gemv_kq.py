@@ -63,9 +63,31 @@ def test_gemv_kq_model_weights(kind, k, n):
     _check(y, oracle.dequant(kind, blocks).reshape(n, k), x)
 
 
+def _q4k_head(h):
+    """ggml Q4_K header bytes [b, 16] -> the decode layout's header: d, dmin
+    unchanged, then per sub-block pair g the 24-bit value
+    sc[2g] | sc[2g+1] << 6 | m[2g] << 12 | m[2g+1] << 18 at bytes 4 + 3g."""
+    s = h[:, 4:16].astype(np.uint32)
+    sc = np.zeros((h.shape[0], 8), np.uint32)
+    mn = np.zeros((h.shape[0], 8), np.uint32)
+    for j in range(4):
+        sc[:, j] = s[:, j] & 63
+        mn[:, j] = s[:, j + 4] & 63
+        sc[:, j + 4] = (s[:, j + 8] & 15) | ((s[:, j] >> 6) << 4)
+        mn[:, j + 4] = (s[:, j + 8] >> 4) | ((s[:, j + 4] >> 6) << 4)
+    out = h.copy()
+    for g in range(4):
+        v = sc[:, 2 * g] | (sc[:, 2 * g + 1] << 6) | (mn[:, 2 * g] << 12) | (mn[:, 2 * g + 1] << 18)
+        for i in range(3):
+            out[:, 4 + 3 * g + i] = (v >> (8 * i)) & 255
+    return out
+
+
 def test_q6k_decode_layout_bytes(rng):
     """The Q6_K decode layout is the 208-byte block bodies, then the f16 d of
-    every block; Q4_K is the blocks unchanged."""
+    every block; Q4_K is two planes, the 128 code bytes of every block, then
+    a 16-byte header per block (d, dmin, and the scales and mins regrouped per
+    sub-block pair)."""
     from rocknpu_b200 import device as dev
     k, n = 1280, 7
     blocks = random_kquant_blocks(6, n * (k // 256), rng)
@@ -76,7 +98,10 @@ def test_q6k_decode_layout_bytes(rng):
     assert np.array_equal(lay[b.shape[0] * 208:].reshape(-1, 2), b[:, 208:])
     b4 = random_kquant_blocks(4, n * (k // 256), rng)
     lay4 = dev.kq_layout(4, torch.from_numpy(b4).cuda(), k, n).cpu().numpy()
-    assert np.array_equal(lay4, b4)
+    b4 = b4.reshape(-1, 144)
+    assert lay4.size == b4.size
+    assert np.array_equal(lay4[:b4.shape[0] * 128].reshape(-1, 128), b4[:, 16:])
+    assert np.array_equal(lay4[b4.shape[0] * 128:].reshape(-1, 16), _q4k_head(b4[:, :16]))
 
 
 def test_gemv_kq_rejects_bad_arguments():
