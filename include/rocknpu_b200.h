@@ -284,8 +284,8 @@ int rocknpu_b200_gemv_w8a8(const int8_t *a_i8, const float *a_scale, const int8_
  * (Q6_K) bytes per weight, the property for which the reference keeps M=1
  * on llama.cpp's K-quant kernels by default (ggml-rocknpu.cpp:305-312).
  * Numerics: each weight is ggml's f32 dequantisation, x is held as 16-bit
- * fixed point per block of 32 values (scale = block max / 32767), the code
- * products are exact int32 sums; outputs are within 1e-3 relative (and about
+ * fixed point per block of 64 (Q4_K: one sub-block pair) or 32 (Q6_K) values
+ * (scale = block max / 32767), the code products are exact int32 sums; outputs are within 1e-3 relative (and about
  * 1e-6 of sum |w x|) of the exact dot product of the f32 weights, not
  * bit-identical to a particular summation order.  A non-finite x sets
  * *status to 1 and leaves y unspecified.  `layout` is the weight's decode

@@ -20,22 +20,21 @@
 // (and which header bits to unpack) never changes, and its 32 x values are
 // read from shared memory once for the R rows.
 //
-// Numerics as in gemv_kq.cu: x is 16-bit fixed point per block of 32 values
-// (X = rint(x * 32767 / max|x|)); per chunk and row the two 16-weight code
-// sums against X are exact int32 dp2a sums; the sub-block scales, mins and
-// d, dmin are applied in f32:
-//   y += d * (sc_a * s_a * S_a + sc_b * s_b / 16 * S_b) - dmin * (m_a * s_a * X_a + m_b * s_b * X_b)
-// over the chunk's two 16-weight halves a (low nibbles) and b (high nibbles,
-// used in place as 16 * code), s the x scales, X_a, X_b the sums of X.
+// Numerics: x is 16-bit fixed point per 64 values, one sub-block pair (X =
+// rint(x * 32767 / max|x|), x ~ X * s); per chunk and row the two 16-weight
+// code sums against X are exact int32 dp2a sums S_a (low nibbles) and S_b
+// (high nibbles, used in place as 16 * code, so the sum is 16 S_b exactly);
+// the 6-bit sub-block scales and mins apply in int32 and d, dmin, s in f32:
+//   y += s * (d * (sc_a * S_a + sc_b * S_b) - dmin * (m_a * X_a + m_b * X_b))
+// with X_a, X_b the sums of X over the chunk's two halves.
 //
 // x in shared memory ("lane order"): chunk c = 8b + j gets 64 bytes, the 16
 // X of its low half then the 16 of its high half, as four 16-byte pieces
 // stored at slots rotated by (c / 2) % 4, so the 8 lanes of a quarter-warp
-// read 8 different bank groups; then per chunk a float4 of constants
-// {s_a, s_b / 16, s_a * X_a, s_b * X_b}.
+// read 8 different bank groups; then per chunk the constants {s, X_a, X_b}.
 //
 // Measured on B200 (cfg5 Q4_K 28672 x 8192, 132 MB, back-to-back calls):
-// 31.3 us, 0.65 of the measured copy bandwidth; the same pipeline without
+// 30.9 us, 0.66 of the measured copy bandwidth; the same pipeline without
 // the arithmetic 28.9 us.  Not kept: per-warp 16-byte cp.async rings of 4 x
 // 512-byte row pieces (35 us: the scattered 512-byte pieces stream at ~3.7
 // TB/s even without arithmetic); loads straight into registers (47 us: too
@@ -155,55 +154,50 @@ __device__ __forceinline__ uint4 ld_stream(const uint4* p) {
     return v;
 }
 
-// x as 16-bit fixed point per block of 32 values into lane order (see the
-// file comment): one 32-value block per thread per pass.
-__device__ void q4k_prepare_x(const Q4Params& p, uint4* xq, float4* cst) {
-    for (int s = threadIdx.x; s < p.k / 32; s += kQ4Threads) {
-        const float4* src = reinterpret_cast<const float4*>(p.x) + 8 * s;
-        float4 v[8];
+// x as 16-bit fixed point per 64 values -- one sub-block pair, i.e. the two
+// halves of the chunks 8b + 2g and 8b + 2g + 1 -- into lane order (see the
+// file comment): one pair per thread per pass.  A chunk's constants are
+// {s, X_a, X_b, 0}: the pair's x scale and the sums of X over the chunk's low
+// and high half, as int32 bits.
+__device__ void q4k_prepare_x(const Q4Params& p, uint4* xq, int4* cst) {
+    for (int s = threadIdx.x; s < p.k / 64; s += kQ4Threads) {
+        const float4* src = reinterpret_cast<const float4*>(p.x) + 16 * s;
+        float4 v[16];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = __ldg(src + i);
+        for (int i = 0; i < 16; ++i) v[i] = __ldg(src + i);
         float m = 0.f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+        for (int i = 0; i < 16; ++i)
             m = fmaxf(m, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
         const bool finite = isfinite(m);
         if (!finite) atomicCAS(p.err, 0, kErrNonFinite);
         const float inv = (finite && m > 0.f) ? 32767.f / m : 0.f;
         const float scale = (finite && m > 0.f) ? m / 32767.f : 0.f;
-        uint32_t packed[16];
-        int half_sum[2] = {0, 0};
+        // values 0..31: sub-block 2g (low nibbles), 32..63: 2g + 1 (high);
+        // quarter qd = 16 values = one half of one sub-block
+        uint32_t packed[32];
+        int qsum[4] = {0, 0, 0, 0};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < 16; ++i) {
             const int q0 = max(-32767, min(32767, __float2int_rn(v[i].x * inv)));
             const int q1 = max(-32767, min(32767, __float2int_rn(v[i].y * inv)));
             const int q2 = max(-32767, min(32767, __float2int_rn(v[i].z * inv)));
             const int q3 = max(-32767, min(32767, __float2int_rn(v[i].w * inv)));
             packed[2 * i] = (static_cast<uint32_t>(q0) & 0xFFFFu) | (static_cast<uint32_t>(q1) << 16);
             packed[2 * i + 1] = (static_cast<uint32_t>(q2) & 0xFFFFu) | (static_cast<uint32_t>(q3) << 16);
-            half_sum[i >> 2] += q0 + q1 + q2 + q3;
+            qsum[i >> 2] += q0 + q1 + q2 + q3;
         }
-        // sub-block s = 8b + js: its half h is the low (js even) or high
-        // (js odd) half of chunk 8b + 2 (js / 2) + h
-        const int b = s >> 3, js = s & 7, odd = js & 1;
+        const int b = s >> 2, g = s & 3;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            const int c = 8 * b + 2 * (js >> 1) + h;
+            const int c = 8 * b + 2 * g + h;  // low half: values 16h.., high half: 32 + 16h..
             const int rot = (c >> 1) & 3;
 #pragma unroll
-            for (int pc = 0; pc < 2; ++pc) {
-                const int piece = 2 * odd + pc;
-                const uint32_t* w = packed + 8 * h + 4 * pc;
+            for (int piece = 0; piece < 4; ++piece) {
+                const uint32_t* w = packed + 16 * (piece >> 1) + 8 * h + 4 * (piece & 1);
                 xq[4 * c + ((piece + rot) & 3)] = make_uint4(w[0], w[1], w[2], w[3]);
             }
-            float* cf = reinterpret_cast<float*>(cst + c);
-            if (odd) {
-                cf[1] = 0.0625f * scale;
-                cf[3] = scale * static_cast<float>(half_sum[h]);
-            } else {
-                cf[0] = scale;
-                cf[2] = scale * static_cast<float>(half_sum[h]);
-            }
+            cst[c] = make_int4(__float_as_int(scale), qsum[h], qsum[2 + h], 0);
         }
     }
 }
@@ -262,13 +256,6 @@ __device__ __forceinline__ float warp_rows(const float (&v)[R], int lane) {
     }
 }
 
-// The low 6 bits of v as a float, exact, on the full-rate pipes (a mask and
-// the 2^23 exponent in one logic operation, then one subtraction) instead of
-// an integer conversion.
-__device__ __forceinline__ float field6(uint32_t v) {
-    return __uint_as_float((v & 63u) | 0x4B000000u) - 8388608.f;
-}
-
 // Lane constants of the unit computation: the lane's sub-block pair
 // g = (lane % 8) / 2 sits at header bytes 4 + 3g .. 6 + 3g, i.e. in words
 // (y, z) for g < 2 and (z, w) otherwise, gathered by one byte permute; and
@@ -285,7 +272,7 @@ struct Q4Lane {
 // partials in acc.
 template <int R>
 __device__ __forceinline__ void q4k_unit(const Q4Params& p, const Q4Lane& ln, const uint4* codes, const uint4* heads,
-                                         const uint4* xq, const float4* cst, int step, int r0, int rows, int lane,
+                                         const uint4* xq, const int4* cst, int step, int r0, int rows, int lane,
                                          float (&acc)[R]) {
     const int c = 32 * step + lane, b = 4 * step + (lane >> 3);
     if (b >= p.nb) {
@@ -295,7 +282,8 @@ __device__ __forceinline__ void q4k_unit(const Q4Params& p, const Q4Lane& ln, co
     }
     const uint4 xa0 = xq[4 * c + ln.s0], xa1 = xq[4 * c + ln.s1];
     const uint4 xb0 = xq[4 * c + ln.s2], xb1 = xq[4 * c + ln.s3];
-    const float4 k4 = cst[c];
+    const int4 k4 = cst[c];  // {x scale bits, X_a, X_b, 0}
+    const float xs = __int_as_float(k4.x);
     const uint4* cq = codes + c;
     const uint4* hq = heads + b;
     const int row_u4 = 8 * p.nb;
@@ -305,12 +293,15 @@ __device__ __forceinline__ void q4k_unit(const Q4Params& p, const Q4Lane& ln, co
         const uint4 q = cq[rr * row_u4];
         const uint4 hw = hq[rr * p.nb];
         const int sa = dot16(q, 0x0F0F0F0Fu, xa0, xa1);
-        const int sb = dot16(q, 0xF0F0F0F0u, xb0, xb1);
+        // high nibbles used in place: every product is 16 x (code x X)
+        const int sb = dot16(q, 0xF0F0F0F0u, xb0, xb1) >> 4;
         const uint32_t v = __byte_perm(ln.zw ? hw.z : hw.y, ln.zw ? hw.w : hw.z, ln.psel);
-        const float qx = fmaf(field6(v), k4.x * static_cast<float>(sa), field6(v >> 6) * (k4.y * static_cast<float>(sb)));
-        const float mx = fmaf(field6(v >> 12), k4.z, field6(v >> 18) * k4.w);
+        // both halves share the pair's x scale: scales and mins apply in
+        // int32 (|sc * S| < 2^29 each, |m * X| < 2^25 each)
+        const int qs = static_cast<int>(v & 63u) * sa + static_cast<int>((v >> 6) & 63u) * sb;
+        const int ms = static_cast<int>((v >> 12) & 63u) * k4.y + static_cast<int>((v >> 18) & 63u) * k4.z;
         const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&hw.x));
-        acc[r] = fmaf(dm.x, qx, -dm.y * mx);
+        acc[r] = xs * fmaf(dm.x, static_cast<float>(qs), -dm.y * static_cast<float>(ms));
     }
 }
 
@@ -339,7 +330,7 @@ __global__ void __launch_bounds__(kQ4Threads, 2) gemv_q4k_kernel(const Q4Params 
     const int code_u4 = p.sr * p.nb * 8, stage_u4 = code_u4 + p.sr * p.nb;
     uint4* ring = smem4;
     uint4* xq = ring + kQ4Stages * stage_u4;                   // [nb * 8][4]
-    float4* cst = reinterpret_cast<float4*>(xq + 32 * p.nb);  // [nb * 8]
+    int4* cst = reinterpret_cast<int4*>(xq + 32 * p.nb);      // [nb * 8]
     float* red = reinterpret_cast<float*>(cst + 8 * p.nb);    // [kQ4Stages][sr][steps]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nstage = (p.n + p.sr - 1) / p.sr;
