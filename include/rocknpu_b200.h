@@ -292,14 +292,17 @@ int rocknpu_b200_gemv_w8a8(const int8_t *a_i8, const float *a_scale, const int8_
  * layout (16-byte aligned, rocknpu_b200_kq_layout); x is 16-byte aligned;
  * k up to 24576 (longer rows return ROCKNPU_STATUS_INVALID_ARGUMENT). */
 size_t rocknpu_b200_kq_layout_bytes(uint32_t kind, size_t k, size_t n);
-/* Write the decode layout of n rows of ggml blocks (device pointers, 16-byte
+/* Write the decode layout of n rows of ggml blocks (device pointers; the
+ * layout 16-byte aligned, Q4_K blocks 16-byte and Q6_K blocks 2-byte
  * aligned): Q4_K two planes, the 128 code bytes of every block [n][k/256]
  * then a 16-byte header per block (the f16 d and dmin, then the 8 scales and
  * 8 mins regrouped per sub-block pair g as the 24-bit value sc[2g] |
- * sc[2g+1] << 6 | m[2g] << 12 | m[2g+1] << 18 at bytes 4 + 3g); Q6_K the
- * 208-byte block bodies (ql, qh, scales) of every row, then the f16 d of
- * every block -- the same 144 / 210 bytes per block, arranged so that every
- * piece is 16-byte aligned. */
+ * sc[2g+1] << 6 | m[2g] << 12 | m[2g+1] << 18 at bytes 4 + 3g); Q6_K 208
+ * bytes per block [n][k/256] -- four 48-byte groups G = 2h + c holding
+ * ql[64h + 16c ..+16], ql[64h + 32 + 16c ..+16], qh[32h + 16c ..+16], then the
+ * 16 scales regrouped so that word G holds sc[8h + c + 2t] in byte t -- then
+ * the f16 d of every block and 16 bytes of padding.  Same bytes per block as
+ * ggml (plus the padding), arranged for 16-byte copies. */
 int rocknpu_b200_kq_layout(uint32_t kind, const uint8_t *blocks, size_t k, size_t n, uint8_t *layout,
                            rocknpu_stream stream);
 int rocknpu_b200_gemv_kq(uint32_t kind, const uint8_t *layout, size_t k, size_t n, const float *x, float *y,

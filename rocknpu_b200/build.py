@@ -24,8 +24,8 @@ LIB = os.path.join(HERE, "librocknpu.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3",
               "--expt-relaxed-constexpr", "-I", INCLUDE]
-SOURCES = ["quant.cu", "gemm.cu", "gemm_plain.cu", "gemm_fused.cu", "gemm_gather.cu", "gemm_pair.cu", "gemv.cu", "gemv_kq.cu", "gemv_q4k.cu", "noalloc.cu", "shard.cu", "capi.cpp", "plugin_rules.cpp", "sidecar.cpp", "synth.cpp", "hostmem.cpp", "plugin_graph.cpp"]
-HEADERS = ["kernels.h", "ptx.cuh", "quant_math.cuh", "gemm_kernel.cuh"]
+SOURCES = ["quant.cu", "gemm.cu", "gemm_plain.cu", "gemm_fused.cu", "gemm_gather.cu", "gemm_pair.cu", "gemv.cu", "gemv_kq.cu", "gemv_q4k.cu", "gemv_q6k.cu", "noalloc.cu", "shard.cu", "capi.cpp", "plugin_rules.cpp", "sidecar.cpp", "synth.cpp", "hostmem.cpp", "plugin_graph.cpp"]
+HEADERS = ["kernels.h", "ptx.cuh", "quant_math.cuh", "gemm_kernel.cuh", "gemv_stage.cuh"]
 
 
 def nvcc() -> str:

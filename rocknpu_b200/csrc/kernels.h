@@ -105,14 +105,18 @@ int launch_gemm_tc(int kind, const void* w, long long ldw_bytes, const void* a, 
 void launch_gemv_w8a8(const int8_t* w, const float* w_scale, const int8_t* a8, const float* a_scale, int k, int n,
                       float* out, cudaStream_t s);
 
-// K5b: M=1 GEMV straight from K-quant blocks (gemv_kq.cu; Q4_K in
-// gemv_q4k.cu).  The decode layout of a Q4_K weight is two planes, the 128
-// code bytes of every block [n][k/256][128] then the 16 header bytes (d,
-// dmin, scales) [n][k/256][16]; of a Q6_K weight, 208-byte block bodies
-// [n][k/256] followed by the f16 d values [n][k/256].
+// K5b: M=1 GEMV straight from K-quant blocks (gemv_kq.cu dispatches to
+// gemv_q4k.cu / gemv_q6k.cu).  The decode layout of a Q4_K weight is two
+// planes, the 128 code bytes of every block [n][k/256][128] then a 16-byte
+// header per block (d, dmin, scales and mins regrouped per sub-block pair);
+// of a Q6_K weight, 208 bytes per block [n][k/256] (four 48-byte groups of
+// ql / qh bytes, then the scales regrouped per group) followed by the f16 d
+// values [n][k/256] and 16 bytes of padding.
 size_t kq_layout_bytes(int kind, size_t k, size_t n);
 int launch_q4k_layout(const uint8_t* blocks, int k, int n, uint8_t* layout, cudaStream_t s);
 int launch_gemv_q4k(const uint8_t* layout, int k, int n, const float* x, float* y, int* err, cudaStream_t s);
+int launch_q6k_layout(const uint8_t* blocks, int k, int n, uint8_t* layout, cudaStream_t s);
+int launch_gemv_q6k(const uint8_t* layout, int k, int n, const float* x, float* y, int* err, cudaStream_t s);
 int launch_kq_layout(int kind, const uint8_t* blocks, int k, int n, uint8_t* layout, cudaStream_t s);
 // y[n] = dequant(W) . x in f32; layout and x 16-byte aligned, k % 256 == 0.
 // Returns a cudaError_t value.

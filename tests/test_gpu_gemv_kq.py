@@ -84,8 +84,9 @@ def _q4k_head(h):
 
 
 def test_q6k_decode_layout_bytes(rng):
-    """The Q6_K decode layout is the 208-byte block bodies, then the f16 d of
-    every block; Q4_K is two planes, the 128 code bytes of every block, then
+    """The Q6_K decode layout is 208 bytes per block (four 48-byte groups of
+    ql / qh bytes, then the 16 scales regrouped per group), then the f16 d of
+    every block and 16 bytes of padding; Q4_K is two planes, the 128 code bytes of every block, then
     a 16-byte header per block (d, dmin, and the scales and mins regrouped per
     sub-block pair)."""
     from rocknpu_b200 import device as dev
@@ -93,9 +94,18 @@ def test_q6k_decode_layout_bytes(rng):
     blocks = random_kquant_blocks(6, n * (k // 256), rng)
     lay = dev.kq_layout(6, torch.from_numpy(blocks).cuda(), k, n).cpu().numpy()
     b = blocks.reshape(-1, 210)
-    assert lay.size == b.shape[0] * 210
-    assert np.array_equal(lay[:b.shape[0] * 208].reshape(-1, 208), b[:, :208])
-    assert np.array_equal(lay[b.shape[0] * 208:].reshape(-1, 2), b[:, 208:])
+    nbt = b.shape[0]
+    assert lay.size == nbt * 210 + 16
+    body = np.zeros((nbt, 208), np.uint8)
+    for G in range(4):
+        h, c = G >> 1, G & 1
+        body[:, 48 * G:48 * G + 16] = b[:, 64 * h + 16 * c:64 * h + 16 * c + 16]
+        body[:, 48 * G + 16:48 * G + 32] = b[:, 64 * h + 32 + 16 * c:64 * h + 48 + 16 * c]
+        body[:, 48 * G + 32:48 * G + 48] = b[:, 128 + 32 * h + 16 * c:128 + 32 * h + 16 * c + 16]
+        for t in range(4):
+            body[:, 192 + 4 * G + t] = b[:, 192 + 8 * h + c + 2 * t]
+    assert np.array_equal(lay[:nbt * 208].reshape(-1, 208), body)
+    assert np.array_equal(lay[nbt * 208:nbt * 210].reshape(-1, 2), b[:, 208:])
     b4 = random_kquant_blocks(4, n * (k // 256), rng)
     lay4 = dev.kq_layout(4, torch.from_numpy(b4).cuda(), k, n).cpu().numpy()
     b4 = b4.reshape(-1, 144)
@@ -116,3 +126,6 @@ def test_gemv_kq_rejects_bad_arguments():
                                   None) == rk.STATUS_INVALID_ARGUMENT  # k % 256
     assert L.rocknpu_b200_gemv_kq(4, lay.data_ptr() + 8, 256, 4, x.data_ptr(), y.data_ptr(), st.data_ptr(),
                                   None) == rk.STATUS_INVALID_ARGUMENT  # unaligned layout
+    for kind in (4, 6):  # rows longer than 24576 are rejected before any work
+        assert L.rocknpu_b200_gemv_kq(kind, lay.data_ptr(), 24576 + 256, 1, x.data_ptr(), y.data_ptr(), st.data_ptr(),
+                                      None) == rk.STATUS_INVALID_ARGUMENT
