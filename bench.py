@@ -948,6 +948,7 @@ def cfg5_block(ms_list, steps, warmup, rank, world, route="peer", check=True):
     # generator: rows [start, start + width) are values [start*K, ...))
     vals = rk.synth_normal(0, width * CFG5_K, 0.02, first=start * CFG5_K).reshape(width, CFG5_K)
     blocks = rk.synth_encode(4, vals)
+    blocks6 = rk.synth_encode(6, vals)  # the same weight as Q6_K, for the K5b Q6_K GEMV
     del vals
     sm = shard.ShardedMatmul(4, blocks, CFG5_K, CFG5_N, route=route, max_m=max_m, blocks_are_local=True)
     gen_s = time.time() - t0
@@ -971,7 +972,8 @@ def cfg5_block(ms_list, steps, warmup, rank, world, route="peer", check=True):
                           "hbm_frac": round(gbytes / (gemv_local * 1e-3) / 1e9 / hbm_peak, 4),
                           "bytes": gbytes}
         # the same M = 1 product straight from this rank's Q4_K blocks (K5b):
-        # 144 bytes per 256 weights instead of 256 + scales
+        # 144 bytes per 256 weights instead of 256 + scales; then from the
+        # same weight encoded as Q6_K (210 bytes per 256 weights)
         if width:
             layout = dev.kq_layout(4, torch.from_numpy(blocks).cuda(), CFG5_K, width)
             xf = x1.reshape(-1).contiguous()
@@ -982,11 +984,24 @@ def cfg5_block(ms_list, steps, warmup, rank, world, route="peer", check=True):
             torch.cuda.synchronize()
             assert kq_status.item() == 0, "gemv_kq status error"
             qbytes = layout.numel() + 4 * CFG5_K + 4 * width
-            res["gemv_q4k"] = {"kernel": "gemv_q4k_kernel (Q4_K code and header planes in bulk-copied row stages, codes and scales applied in registers, dp2a)",
+            res["gemv_q4k"] = {"kernel": "kq::stage_kernel<Q4Fmt> (Q4_K code and header planes in bulk-copied row stages, codes and scales applied in registers, dp2a)",
                                "us_local": round(kq_ms * 1e3, 2),
                                "gbs_local": round(qbytes / (kq_ms * 1e-3) / 1e9, 1),
                                "hbm_frac": round(qbytes / (kq_ms * 1e-3) / 1e9 / hbm_peak, 4),
                                "bytes": qbytes, "vs_gemv_w8": round(gemv_local / kq_ms, 3)}
+            del layout
+            # and from Q6_K blocks of the same shape (210 bytes per 256 weights)
+            layout = dev.kq_layout(6, torch.from_numpy(blocks6).cuda(), CFG5_K, width)
+            q6_ms = _timed(lambda: dev.gemv_kq(6, layout, xf, width, kq_status, out=yq), max(steps, 50), warmup,
+                           dist)
+            torch.cuda.synchronize()
+            assert kq_status.item() == 0, "gemv_kq status error"
+            q6bytes = width * (CFG5_K // 256) * 210 + 4 * CFG5_K + 4 * width
+            res["gemv_q6k"] = {"kernel": "kq::stage_kernel<Q6Fmt> (Q6_K ql/qh groups and d plane in bulk-copied row stages, dp2a)",
+                               "us_local": round(q6_ms * 1e3, 2),
+                               "gbs_local": round(q6bytes / (q6_ms * 1e-3) / 1e9, 1),
+                               "hbm_frac": round(q6bytes / (q6_ms * 1e-3) / 1e9 / hbm_peak, 4),
+                               "bytes": q6bytes}
             del layout, yq
         for m in ms_list:
             x = cfg5_activations(m)
