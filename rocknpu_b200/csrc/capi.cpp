@@ -187,6 +187,34 @@ struct DevBuf {
     }
 };
 
+// Page-locked host memory, grown like DevBuf; the owner makes sure no copy
+// that uses it is in flight when it grows or is released.
+struct HostBuf {
+    void* ptr = nullptr;
+    size_t cap = 0;
+    cudaError_t ensure(size_t bytes) {
+        if (bytes <= cap) return cudaSuccess;
+        release();
+        const size_t want = round_up(bytes + bytes / 4, 64 << 10);
+        const cudaError_t e = cudaHostAlloc(&ptr, want, cudaHostAllocDefault);
+        if (e != cudaSuccess) {
+            ptr = nullptr;
+            return e;
+        }
+        cap = want;
+        return cudaSuccess;
+    }
+    void release() {
+        if (ptr) cudaFreeHost(ptr);
+        ptr = nullptr;
+        cap = 0;
+    }
+    template <class T>
+    T* as() const {
+        return static_cast<T*>(ptr);
+    }
+};
+
 // Resident prepared int8 rows [n][k] + per-row scales [n].
 struct PreparedW8 {
     int8_t* w = nullptr;
@@ -198,6 +226,18 @@ struct PreparedW8 {
         if (scales) cudaFree(scales);
     }
     size_t bytes() const { return n * k + n * sizeof(float); }
+};
+
+// Resident K5b decode layout of one Q4_K / Q6_K weight (rk::kq_layout_bytes
+// bytes, built by rk::launch_kq_layout from the K-quant blocks).
+struct PreparedKq {
+    uint8_t* layout = nullptr;
+    int kind = 0;
+    size_t n = 0, k = 0, len = 0;
+    ~PreparedKq() {
+        if (layout) cudaFree(layout);
+    }
+    size_t bytes() const { return len; }
 };
 
 // Resident f16 rows [n][ld].
@@ -225,6 +265,7 @@ struct Key {
 using KeyList = std::vector<Key>;
 using W8Ptr = std::shared_ptr<PreparedW8>;
 using F16Ptr = std::shared_ptr<PreparedF16>;
+using KqPtr = std::shared_ptr<PreparedKq>;
 
 uint64_t now_ns() {
     return static_cast<uint64_t>(
@@ -250,6 +291,12 @@ struct RockNpuContext {
     DevBuf gemm_ws;      // split-K workspace, all-zero between launches
     DevBuf quant_sync;   // fused-quantiser counters, all-zero between launches
     DevBuf hilo_a, hilo_out;  // HILO stacked activations [2m][k], summed outputs
+    // M=1 staging, device and page-locked host blocks with one layout,
+    // [y: outputs][status word, 16 bytes][x: k floats]: a call copies the
+    // zeroed status word and x in with one copy, and y with the status out
+    // with one copy (m1_call).
+    DevBuf m1_dev;
+    HostBuf m1_host;
     bool in_hilo = false;     // inside a HILO-encoded call (HiloInner, L:2025-2043)
 
     // Prompt-path (M-tile) resident weights: single projections and
@@ -260,6 +307,11 @@ struct RockNpuContext {
     // L:3264-3600).
     std::map<Key, W8Ptr> decode;
     std::map<KeyList, W8Ptr> decode_groups;
+    // Opt-in K5b decode route (ROCKNPU_B200_DECODE_KQ at creation): M=1
+    // Q4_K / Q6_K members are served from decode layouts of their K-quant
+    // bytes, one cached layout per member key.
+    bool decode_kq = false;
+    std::map<Key, KqPtr> kq;
     // FP16 executor weights and the FP16 route's dequantised weights.
     std::map<Key, F16Ptr> f16;
 
@@ -492,6 +544,51 @@ void zero_copy_mode(bool* in, bool* out) {
     }
 }
 
+// One M=1 call from host buffers, for both decode routes: x and a zeroed
+// status word go in with one copy from the page-locked staging block, the
+// kernels queued by `launch(x, y, err)` run on c->stream, y and the status
+// come back with one copy, and the host waits once.  Each copy or memset in
+// a stream costs the call a few microseconds on B200, so the sequence has
+// three operations (copy, kernels, copy) where the general path has seven.
+// On an error the caller's outputs are untouched; a non-finite x is
+// INVALID_ARGUMENT, as on the general path.
+template <class Launch>
+int m1_call(Ctx* c, const float* a, size_t k, const OutSeg* segs, size_t nseg, bool overlap, Launch&& launch) {
+    size_t total = 0;
+    for (size_t i = 0; i < nseg; ++i) total += segs[i].n;
+    const size_t y_bytes = round_up(total * sizeof(float), 16);
+    const size_t bytes = y_bytes + 16 + k * sizeof(float);
+    if (c->m1_dev.ensure(bytes) != cudaSuccess || c->m1_host.ensure(bytes) != cudaSuccess) return kExecError;
+    uint8_t* hb = c->m1_host.as<uint8_t>();
+    uint8_t* db = c->m1_dev.as<uint8_t>();
+    int* h_st = reinterpret_cast<int*>(hb + y_bytes);
+    std::memset(h_st, 0, 16);
+    std::memcpy(hb + y_bytes + 16, a, k * sizeof(float));
+    if (cudaMemcpyAsync(db + y_bytes, hb + y_bytes, 16 + k * sizeof(float), cudaMemcpyHostToDevice, c->stream))
+        return kExecError;
+    if (launch(reinterpret_cast<const float*>(db + y_bytes + 16), reinterpret_cast<float*>(db),
+               reinterpret_cast<int*>(db + y_bytes)) != cudaSuccess)
+        return kExecError;
+    if (overlap && c->overlap) {
+        // one-shot host work while the GPU runs (take_overlap, L:264-273)
+        rocknpu_overlap_fn fn = c->overlap;
+        void* user = c->overlap_user;
+        c->overlap = nullptr;
+        c->overlap_user = nullptr;
+        fn(user);
+    }
+    if (cudaMemcpyAsync(hb, db, y_bytes + 16, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess) return kExecError;
+    if (wait_stream(c->stream) != cudaSuccess) return kExecError;
+    const int s = *h_st;
+    if (s != rk::kErrNone) return s == rk::kErrNonFinite ? kInvalid : kExecError;
+    const float* y = reinterpret_cast<const float*>(hb);
+    for (size_t i = 0; i < nseg; ++i) {
+        std::memcpy(segs[i].host, y, segs[i].n * sizeof(float));
+        y += segs[i].n;
+    }
+    return kOk;
+}
+
 // Quantisation + GEMM (GEMV for m == 1) of host activations against a
 // resident int8 weight, member outputs copied back, pipelined over row
 // chunks on three streams.  Page-locked, device-mapped host buffers are not
@@ -506,6 +603,14 @@ int run_w8a8(Ctx* c, const PreparedW8& pw, const float* host_a, size_t m, size_t
              bool m1_overlap, const float* dev_a = nullptr, bool keep = false) {
     const size_t ld8 = round_up(k, 16);
     const size_t total_n = pw.n;
+    if (m == 1 && k % 16 == 0 && !dev_a) {
+        // K2 + K5 fused into one launch (the row quantiser's bits)
+        return m1_call(c, host_a, k, segs, nseg, m1_overlap, [&](const float* x, float* y, int* err) {
+            rk::launch_gemv_w8a8_x(pw.w, pw.scales, x, static_cast<int>(k), static_cast<int>(total_n), y, err,
+                                   c->stream);
+            return cudaGetLastError();
+        });
+    }
     if ((!dev_a && c->a_f32.ensure(m * k * sizeof(float))) || c->a_i8.ensure(m * ld8) ||
         c->a_scale.ensure(m * sizeof(float)) || c->out_f32.ensure(m * total_n * sizeof(float)))
         return kExecError;
@@ -542,32 +647,6 @@ int run_w8a8(Ctx* c, const PreparedW8& pw, const float* host_a, size_t m, size_t
     float* a_dev = c->a_f32.as<float>();
     int8_t* a8 = c->a_i8.as<int8_t>();
     float* as = c->a_scale.as<float>();
-
-    if (m == 1 && k % 16 == 0) {
-        if (cudaMemcpyAsync(a_dev, host_a, k * sizeof(float), cudaMemcpyHostToDevice, c->stream)) return kExecError;
-        rk::launch_quant_rows(a_dev, 1, static_cast<int>(k), static_cast<long long>(k), a8,
-                              static_cast<long long>(ld8), as, c->d_status, c->stream);
-        rk::launch_gemv_w8a8(pw.w, pw.scales, a8, as, static_cast<int>(k), static_cast<int>(total_n), out, c->stream);
-        if (cudaGetLastError() != cudaSuccess) return kExecError;
-        if (m1_overlap && c->overlap) {
-            // one-shot host work while the GPU runs (take_overlap, L:264-273)
-            rocknpu_overlap_fn fn = c->overlap;
-            void* user = c->overlap_user;
-            c->overlap = nullptr;
-            c->overlap_user = nullptr;
-            fn(user);
-        }
-        st = finish(c);
-        if (st != kOk) return st;
-        size_t start = 0;
-        for (size_t i = 0; i < nseg; ++i) {
-            if (cudaMemcpyAsync(segs[i].host, out + start, segs[i].n * sizeof(float), cudaMemcpyDeviceToHost,
-                                c->stream))
-                return kExecError;
-            start += segs[i].n;
-        }
-        return cuda_status(wait_stream(c->stream));
-    }
 
     const uint64_t t_issue = c->profile ? now_ns() : 0;
     bool zin = false, zout = false;
@@ -763,10 +842,89 @@ int q_prompt_f16(Ctx* c, int kind, const uint8_t* w, size_t bytes, const float* 
     return run_f16(c, *p, a, m, k, out, dev_a, keep);
 }
 
+// One member's K5b decode layout from its K-quant bytes (staged through
+// c->staging, repacked by rk::launch_kq_layout).
+int build_kq(Ctx* c, const Member& mb, size_t k, KqPtr& out) {
+    auto p = std::make_shared<PreparedKq>();
+    p->kind = mb.kind;
+    p->n = mb.n;
+    p->k = k;
+    p->len = rk::kq_layout_bytes(mb.kind, k, mb.n);
+    if (p->len == 0) return kInvalid;
+    if (cudaMalloc(&p->layout, p->len) != cudaSuccess) return kExecError;
+    if (c->staging.ensure(mb.bytes) != cudaSuccess) return kExecError;
+    if (cudaMemcpyAsync(c->staging.ptr, mb.host, mb.bytes, cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
+        return kExecError;
+    if (rk::launch_kq_layout(mb.kind, c->staging.as<uint8_t>(), static_cast<int>(k), static_cast<int>(mb.n),
+                             p->layout, c->stream) != cudaSuccess)
+        return kExecError;
+    const int st = cuda_status(wait_stream(c->stream));
+    if (st != kOk) return st;
+    out = std::move(p);
+    return kOk;
+}
+
+// The K5b route applies to M=1 calls whose members are all Q4_K / Q6_K
+// bytes, when the context was created with ROCKNPU_B200_DECODE_KQ set and K
+// is within the GEMV's limit (24576).  Other calls keep the W8A8 route.
+bool kq_route(const Ctx* c, const Member* members, size_t count, size_t k) {
+    if (!c->decode_kq || k > 24576) return false;
+    for (size_t i = 0; i < count; ++i)
+        if (members[i].kind != rk::kQ4K && members[i].kind != rk::kQ6K) return false;
+    return true;
+}
+
+// M=1 on the K5b route: the GEMV reads the cached decode layouts (0.5625 B
+// per weight for Q4_K, 0.82 for Q6_K, against 1 B of int8 rows) and returns
+// f32 results within 1e-3 of the exact product of the dequantised weights
+// and x, instead of the W8A8 route's bits.  Cache statistics count a call as
+// a hit when every member's layout was resident.
+int decode_kq_m1(Ctx* c, const KeyList& keys, const Member* members, size_t count, const float* a, OutSeg* segs,
+                 size_t k) {
+    const uint64_t t0 = now_ns();
+    KqPtr p[4];
+    bool hit = true;
+    size_t total = 0;
+    for (size_t i = 0; i < count; ++i) {
+        total += members[i].n;
+        auto it = c->kq.find(keys[i]);
+        if (it != c->kq.end()) {
+            p[i] = it->second;
+            continue;
+        }
+        hit = false;
+        const int st = build_kq(c, members[i], k, p[i]);
+        if (st != kOk) return st;
+        c->kq.emplace(keys[i], p[i]);
+    }
+    if (!hit) c->m1_shapes.insert({k, total});
+    const int st = m1_call(c, a, k, segs, count, true, [&](const float* x, float* y, int* err) {
+        for (size_t i = 0; i < count; ++i) {
+            const int e = rk::launch_gemv_kq(p[i]->kind, p[i]->layout, static_cast<int>(k), static_cast<int>(p[i]->n),
+                                             x, y, err, c->stream);
+            if (e != cudaSuccess) return static_cast<cudaError_t>(e);
+            y += p[i]->n;
+        }
+        return cudaSuccess;
+    });
+    if (st != kOk) return st;
+    const uint64_t dt = now_ns() - t0;
+    c->m1_calls++;
+    if (hit) {
+        c->hits++;
+        c->hit_ns += dt;
+    } else {
+        c->misses++;
+        c->miss_ns += dt;
+    }
+    return kOk;
+}
+
 // M=1 through the decode cache (execute_cached_w8a8_m1, L:1567-1701 and the
 // pair/triple forms, L:3264-3600); `members` are concatenated along N.
 int decode_m1(Ctx* c, const KeyList& keys, const Member* members, size_t count, const float* a, OutSeg* segs,
               size_t k) {
+    if (kq_route(c, members, count, k)) return decode_kq_m1(c, keys, members, count, a, segs, k);
     const uint64_t t0 = now_ns();
     W8Ptr p;
     bool hit = false;
@@ -978,6 +1136,7 @@ rocknpu_context* rocknpu_context_create(void) {
     c->device = dev;
     c->direct_submit = std::getenv("ROCKNPU_W8_DIRECT_SUBMIT") != nullptr;
     c->profile = env_enabled("ROCKNPU_MTILE_PROFILE");
+    c->decode_kq = env_enabled("ROCKNPU_B200_DECODE_KQ");
     c->gemm_ws.zeroed = true;
     c->quant_sync.zeroed = true;
     bool events_ok = true;
@@ -1002,10 +1161,11 @@ int rocknpu_context_decode_cache_stats(const rocknpu_context* context, rocknpu_d
     size_t resident = 0;
     for (auto& kv : c->decode) resident += kv.second->bytes();
     for (auto& kv : c->decode_groups) resident += kv.second->bytes();
+    for (auto& kv : c->kq) resident += kv.second->bytes();
     rocknpu_decode_cache_stats s{};
     s.hits = c->hits;
     s.misses = c->misses;
-    s.entries = c->decode.size() + c->decode_groups.size();
+    s.entries = c->decode.size() + c->decode_groups.size() + c->kq.size();
     s.resident_bytes = resident;
     s.hit_ns = c->hit_ns;
     s.miss_ns = c->miss_ns;
@@ -1034,10 +1194,12 @@ void rocknpu_context_destroy(rocknpu_context* context) {
     c->groups.clear();
     c->decode.clear();
     c->decode_groups.clear();
+    c->kq.clear();
     c->f16.clear();
     for (DevBuf* b : {&c->a_f32, &c->a_i8, &c->a_scale, &c->a_f16, &c->out_f32, &c->staging,
-                      &c->gemm_ws, &c->quant_sync, &c->hilo_a, &c->hilo_out})
+                      &c->gemm_ws, &c->quant_sync, &c->hilo_a, &c->hilo_out, &c->m1_dev})
         b->release();
+    c->m1_host.release();
     if (c->d_status) cudaFree(c->d_status);
     if (c->h_status) cudaFreeHost(c->h_status);
     for (int i = 0; i < RockNpuContext::kMaxChunks; ++i) {
@@ -1421,6 +1583,10 @@ int rocknpu_b200_matmul_w8a8(rocknpu_context* context, const float* a, const int
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : context->stream;
     const size_t ld8 = round_up(k, 16);
     if (context->a_i8.ensure(m * ld8) || context->a_scale.ensure(m * sizeof(float))) return kExecError;
+    if (m == 1 && k % 16 == 0 && reinterpret_cast<uintptr_t>(a) % 16 == 0) {
+        rk::launch_gemv_w8a8_x(w_i8, w_scales, a, static_cast<int>(k), static_cast<int>(n), out, context->d_status, s);
+        return cuda_status(cudaGetLastError());
+    }
     if (m == 1 && k % 16 == 0) {
         rk::launch_quant_rows(a, 1, static_cast<int>(k), static_cast<long long>(k), context->a_i8.as<int8_t>(),
                               static_cast<long long>(ld8), context->a_scale.as<float>(), context->d_status, s);

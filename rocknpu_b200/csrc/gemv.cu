@@ -6,6 +6,8 @@
 // no-L1-allocate loads, four dp4a per chunk, an exact int32 warp sum, and
 // lane 0 applies the reference's rescale (f32(acc) * a_scale) * w_scale.
 #include "kernels.h"
+#include "ptx.cuh"
+#include "quant_math.cuh"
 
 namespace rk {
 namespace {
@@ -21,15 +23,11 @@ __device__ __forceinline__ int4 ld_stream(const int4* p) {
     return v;
 }
 
-__global__ void __launch_bounds__(kGemvThreads) gemv_w8a8_kernel(const int8_t* __restrict__ w,
-                                                                  const float* __restrict__ w_scale,
-                                                                  const int8_t* __restrict__ a8,
-                                                                  const float* __restrict__ a_scale, int k, int n,
-                                                                  float* __restrict__ out) {
-    extern __shared__ int4 sa[];
+// Rows of one CTA against the quantised activation staged in shared memory.
+__device__ __forceinline__ void gemv_rows(const int4* sa, const int8_t* __restrict__ w,
+                                          const float* __restrict__ w_scale, float a_scale, int k, int n,
+                                          float* __restrict__ out) {
     const int chunks = k >> 4;
-    for (int i = threadIdx.x; i < chunks; i += kGemvThreads) sa[i] = reinterpret_cast<const int4*>(a8)[i];
-    __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * kRowsPerCta + warp;
     if (row >= n) return;
@@ -52,7 +50,58 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_w8a8_kernel(const int8_t* _
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) out[row] = __fmul_rn(__fmul_rn(__int2float_rn(acc), *a_scale), w_scale[row]);
+    if (lane == 0) out[row] = __fmul_rn(__fmul_rn(__int2float_rn(acc), a_scale), w_scale[row]);
+}
+
+__global__ void __launch_bounds__(kGemvThreads) gemv_w8a8_kernel(const int8_t* __restrict__ w,
+                                                                  const float* __restrict__ w_scale,
+                                                                  const int8_t* __restrict__ a8,
+                                                                  const float* __restrict__ a_scale, int k, int n,
+                                                                  float* __restrict__ out) {
+    extern __shared__ int4 sa[];
+    const int chunks = k >> 4;
+    for (int i = threadIdx.x; i < chunks; i += kGemvThreads) sa[i] = reinterpret_cast<const int4*>(a8)[i];
+    __syncthreads();
+    gemv_rows(sa, w, w_scale, *a_scale, k, n, out);
+}
+
+// K2 + K5 in one launch for M=1: every CTA quantises the f32 activation x
+// (16-byte aligned, k % 16 == 0) into shared memory with the row quantiser's
+// arithmetic -- the same absmax (a max is order-independent), scale and
+// per-value rounding, so the same bits -- then runs the rows above.  The
+// repeated work per CTA is one 4k-byte read of x (L2-resident after the
+// first CTAs) and a block reduction.  A non-finite x sets kErrNonFinite and
+// no output is written.
+__global__ void __launch_bounds__(kGemvThreads) gemv_w8a8_x_kernel(const int8_t* __restrict__ w,
+                                                                    const float* __restrict__ w_scale,
+                                                                    const float* __restrict__ x, int k, int n,
+                                                                    float* __restrict__ out, int* err) {
+    extern __shared__ int4 sa[];
+    __shared__ float red[kGemvThreads / 32];
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    const int k4 = k >> 2;
+    float amax = 0.0f;
+    bool finite = true;
+    for (int i = threadIdx.x; i < k4; i += kGemvThreads) {
+        const float4 v = __ldg(x4 + i);
+        finite &= isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w);
+        amax = fmaxf(fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y))), fmaxf(fabsf(v.z), fabsf(v.w)));
+    }
+    if (__syncthreads_or(!finite)) {
+        if (threadIdx.x == 0) atomicExch(err, kErrNonFinite);
+        return;
+    }
+    amax = warp_max(amax);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    float m = red[0];
+#pragma unroll
+    for (int i = 1; i < kGemvThreads / 32; ++i) m = fmaxf(m, red[i]);
+    const float scale = row_scale(m), inv = row_inv(scale);
+    uint32_t* sa32 = reinterpret_cast<uint32_t*>(sa);
+    for (int i = threadIdx.x; i < k4; i += kGemvThreads) sa32[i] = quant_pack4(__ldg(x4 + i), scale, inv);
+    __syncthreads();
+    gemv_rows(sa, w, w_scale, scale, k, n, out);
 }
 
 }  // namespace
@@ -64,6 +113,15 @@ void launch_gemv_w8a8(const int8_t* w, const float* w_scale, const int8_t* a8, c
         cudaFuncSetAttribute(gemv_w8a8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     gemv_w8a8_kernel<<<(n + kRowsPerCta - 1) / kRowsPerCta, kGemvThreads, smem, s>>>(w, w_scale, a8, a_scale, k, n,
                                                                                      out);
+}
+
+void launch_gemv_w8a8_x(const int8_t* w, const float* w_scale, const float* x, int k, int n, float* out, int* err,
+                        cudaStream_t s) {
+    const size_t smem = static_cast<size_t>(k);
+    if (smem > 48 * 1024)
+        cudaFuncSetAttribute(gemv_w8a8_x_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    gemv_w8a8_x_kernel<<<(n + kRowsPerCta - 1) / kRowsPerCta, kGemvThreads, smem, s>>>(w, w_scale, x, k, n, out,
+                                                                                       err);
 }
 
 }  // namespace rk

@@ -495,6 +495,46 @@ def test_quantisers_round_like_the_ieee_quotient_near_half_integers(ctx, rng, mo
     assert np.array_equal(_bits(out.cpu().numpy()), _bits(ref))
 
 
+@pytest.mark.parametrize("case", ["normal", "outliers", "zero", "near_half", "subnormal"])
+@pytest.mark.parametrize("k,n", [(2048, 2048), (5632, 256), (512, 32), (16384, 72)])
+def test_gemv_fused_quant_m1_bit_exact(ctx, dev, rng, case, k, n):
+    """M=1 through the context's device entry: the quantiser runs inside the
+    GEMV (one launch), with the row quantiser's bits."""
+    if case == "near_half":
+        x = _near_half_rows(rng, 1, k)[0]
+    elif case == "zero":
+        x = np.zeros(k, np.float32)
+    elif case == "subnormal":
+        x = (rng.standard_normal(k) * 1e-39).astype(np.float32)
+    else:
+        x = rng.standard_normal(k).astype(np.float32)
+        if case == "outliers":
+            x[rng.choice(k, max(1, k // 100), replace=False)] *= 20.0
+    w8 = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
+    ws = rng.uniform(1e-3, 1e-2, size=n).astype(np.float32)
+    st, ref = oracle.matmul_w8a8(w8, ws, x.reshape(1, k))
+    assert st == 0
+    out = torch.full((1, n), float("nan"), device="cuda")
+    dev.matmul_w8a8(ctx, torch.from_numpy(x.reshape(1, k)).cuda(), torch.from_numpy(w8).cuda(),
+                    torch.from_numpy(ws).cuda(), out)
+    assert rk.lib().rocknpu_b200_context_check(ctx.handle) == 0
+    assert np.array_equal(_bits(out.cpu().numpy()), _bits(ref))
+
+
+def test_gemv_fused_quant_m1_flags_non_finite(ctx, dev, rng):
+    k, n = 2048, 64
+    w8 = torch.from_numpy(rng.integers(-127, 128, size=(n, k), dtype=np.int8)).cuda()
+    ws = torch.from_numpy(rng.uniform(1e-3, 1e-2, size=n).astype(np.float32)).cuda()
+    x = rng.standard_normal((1, k)).astype(np.float32)
+    x[0, 1234] = np.nan
+    out = torch.empty((1, n), device="cuda")
+    dev.matmul_w8a8(ctx, torch.from_numpy(x).cuda(), w8, ws, out)
+    assert rk.lib().rocknpu_b200_context_check(ctx.handle) == rk.STATUS_INVALID_ARGUMENT
+    x[0, 1234] = 0.5
+    dev.matmul_w8a8(ctx, torch.from_numpy(x).cuda(), w8, ws, out)
+    assert rk.lib().rocknpu_b200_context_check(ctx.handle) == 0
+
+
 # ---- HILO two-part activations (ROCKNPU_PREFILL_HILO) -------------------------
 
 def _prepared(kind, blocks, k, n):
