@@ -153,7 +153,11 @@ int rocknpu_matmul_w8a8_triple_f32_f32_m1(rocknpu_context *context, const int8_t
                                           float *second_output_f32, float *third_output_f32, size_t k);
 
 /* Two M=1 Q projections (kinds 4/6) sharing one activation (H:159-172,
- * L:4633-4717). */
+ * L:4633-4717).  B200 option: with ROCKNPU_B200_DECODE_KQ set when the
+ * context is created, the M=1 K-quant calls (this one, the triple, and the
+ * Q4_K / Q6_K entries at m == 1, k <= 24576) run the K-quant decode GEMV on
+ * cached decode layouts: f32 results within 1e-3 relative of the exact
+ * product instead of the W8A8 bits. */
 int rocknpu_matmul_q_pair_f32_f32_m1(rocknpu_context *context, const uint8_t *first_weights, size_t first_bytes,
                                      uint32_t first_kind, size_t first_n, const uint8_t *second_weights,
                                      size_t second_bytes, uint32_t second_kind, size_t second_n,
