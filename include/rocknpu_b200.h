@@ -294,7 +294,9 @@ int rocknpu_b200_gemv_w8a8(const int8_t *a_i8, const float *a_scale, const int8_
 size_t rocknpu_b200_kq_layout_bytes(uint32_t kind, size_t k, size_t n);
 /* Write the decode layout of n rows of ggml blocks (device pointers; the
  * layout 16-byte aligned, Q4_K blocks 16-byte and Q6_K blocks 2-byte
- * aligned): Q4_K two planes, the 128 code bytes of every block [n][k/256]
+ * aligned): Q4_K two planes, the 128 * k/256 qs bytes of every row [n] --
+ * regrouped per step of 8 blocks (nbs blocks in a short last step): 16-byte
+ * chunk j of the step's block i at slot (j % 2) * 4 nbs + 4 i + j / 2 --
  * then a 16-byte header per block (the f16 d and dmin, then the 8 scales and
  * 8 mins regrouped per sub-block pair g as the 24-bit value sc[2g] |
  * sc[2g+1] << 6 | m[2g] << 12 | m[2g+1] << 18 at bytes 4 + 3g); Q6_K 208

@@ -149,7 +149,7 @@ struct Q6Fmt {
     // One unit: step `step` (group G of block 8 step + lane / 4) of stage
     // rows r0 .. r0 + R - 1; rows past the stage's end repeat its last row
     // (their sums are never read).
-    template <int R>
+    template <int R, bool Full>
     __device__ static void unit(const kq::StageParams& p, const Lane& ln, const uint8_t* codes, const uint8_t* heads,
                                 const uint8_t* xsm, int step, int r0, int rows, int lane, float (&acc)[R]) {
         const int cc = 32 * step + lane, b = 8 * step + (lane >> 2);
@@ -170,6 +170,8 @@ struct Q6Fmt {
         const __half* dv = reinterpret_cast<const __half*>(heads);
 #pragma unroll
         for (int r = 0; r < R; ++r) {
+            // rows past a short stage's end repeat its last row (their sums
+            // are never read); measured faster here than skipping them
             const int rr = min(r0 + r, rows - 1);
             const uint8_t* blk = codes + (static_cast<size_t>(rr) * p.nb + b) * 208;
             const uint4 A = *reinterpret_cast<const uint4*>(blk + 48 * ln.G);

@@ -86,9 +86,7 @@ def _q4k_head(h):
 def test_q6k_decode_layout_bytes(rng):
     """The Q6_K decode layout is 208 bytes per block (four 48-byte groups of
     ql / qh bytes, then the 16 scales regrouped per group), then the f16 d of
-    every block and 16 bytes of padding; Q4_K is two planes, the 128 code bytes of every block, then
-    a 16-byte header per block (d, dmin, and the scales and mins regrouped per
-    sub-block pair)."""
+    every block and 16 bytes of padding."""
     from rocknpu_b200 import device as dev
     k, n = 1280, 7
     blocks = random_kquant_blocks(6, n * (k // 256), rng)
@@ -106,12 +104,29 @@ def test_q6k_decode_layout_bytes(rng):
             body[:, 192 + 4 * G + t] = b[:, 192 + 8 * h + c + 2 * t]
     assert np.array_equal(lay[:nbt * 208].reshape(-1, 208), body)
     assert np.array_equal(lay[nbt * 208:nbt * 210].reshape(-1, 2), b[:, 208:])
-    b4 = random_kquant_blocks(4, n * (k // 256), rng)
+
+
+@pytest.mark.parametrize("k", [1280, 2560, 4096])
+def test_q4k_decode_layout_bytes(rng, k):
+    """Q4_K: two planes.  The code plane keeps each row's 128 * nb qs bytes,
+    regrouped per step of 8 blocks (a short last step has nbs < 8): chunk j
+    (qs bytes 16j .. 16j + 15) of the step's block i goes to 16-byte slot
+    (j % 2) * 4 nbs + 4 i + j // 2.  Then a 16-byte header per block (d,
+    dmin, and the scales and mins regrouped per sub-block pair)."""
+    from rocknpu_b200 import device as dev
+    n, nb = 7, k // 256
+    b4 = random_kquant_blocks(4, n * nb, rng)
     lay4 = dev.kq_layout(4, torch.from_numpy(b4).cuda(), k, n).cpu().numpy()
-    b4 = b4.reshape(-1, 144)
+    b4 = b4.reshape(n, nb, 144)
     assert lay4.size == b4.size
-    assert np.array_equal(lay4[:b4.shape[0] * 128].reshape(-1, 128), b4[:, 16:])
-    assert np.array_equal(lay4[b4.shape[0] * 128:].reshape(-1, 16), _q4k_head(b4[:, :16]))
+    want = np.zeros((n, nb * 8, 16), np.uint8)
+    for b in range(nb):
+        t, i = divmod(b, 8)
+        nbs = min(8, nb - 8 * t)
+        for j in range(8):
+            want[:, 64 * t + (j % 2) * 4 * nbs + 4 * i + j // 2] = b4[:, b, 16 + 16 * j:32 + 16 * j]
+    assert np.array_equal(lay4[:n * nb * 128].reshape(n, nb * 8, 16), want)
+    assert np.array_equal(lay4[n * nb * 128:].reshape(-1, 16), _q4k_head(b4.reshape(-1, 144)[:, :16]))
 
 
 def test_gemv_kq_rejects_bad_arguments():
