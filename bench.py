@@ -563,6 +563,12 @@ def run_ours(args, rank: int, world: int):
                "path": "rocknpu_matmul_q_concat_f32_f32_mtile + rocknpu_matmul_q{4,6}_k_f32_f32, "
                        "rocknpu_b200_host_alloc host buffers"}
 
+    # configs[1]'s decode steps: every rank decodes on its own GPU (M = 1
+    # calls do not shard), rank 0 reports
+    dec = None
+    if not args.no_decode and MODEL == "tinyllama":
+        dec = decode_block(weights, DECODE_TOKENS, args.warmup)
+
     if dist is not None:
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -604,6 +610,7 @@ def run_ours(args, rank: int, world: int):
         "roofline": roof,
         "pp128": short,
         "e2e": e2e,
+        "decode": dec,
         "cpu_baseline": cpu,
         "gpu_launches": launches_per_step * args.steps if launches_per_step is not None else None,
         "launches_per_step": launches_per_step,
@@ -614,6 +621,109 @@ def run_ours(args, rank: int, world: int):
     if big is not None:
         line["cfg5" if world == 1 else "shard"] = big
     return line
+
+
+DECODE_TOKENS = 128  # configs[1]: 128 decode steps after the prompt
+
+
+def decode_plan():
+    """The plugin's M=1 calls per layer with its decode switch on
+    (ROCKNPU_DECODE=npu, ggml-rocknpu.cpp:313-322): [(call, [(kind, n)], k)]
+    -- the QKV triple (q, v, k), o, the gate/up pair, down."""
+    from rocknpu_b200 import plugin
+    old = os.environ.get("ROCKNPU_DECODE")
+    os.environ["ROCKNPU_DECODE"] = "npu"
+    try:
+        spec = {"hidden": HIDDEN, "ffn": FFN, "kv": KV}
+        out = []
+        for calls in plugin.layer_calls(spec, 1, LAYERS):
+            out.append([(c, [(name, plugin.TYPE_TO_KIND[t], n) for (name, t, n) in members], k)
+                        for c, members, k in calls])
+        return out
+    finally:
+        if old is None:
+            os.environ.pop("ROCKNPU_DECODE", None)
+        else:
+            os.environ["ROCKNPU_DECODE"] = old
+
+
+def decode_block(weights, tokens, warmup):
+    """TinyLlama-shape decode (configs[1]'s decode steps): per token the
+    plugin's 88 M=1 calls (decode_plan) through the reference's M=1 entry
+    points from page-locked host buffers, on the default W8A8 route and on
+    the opt-in K5b route (ROCKNPU_B200_DECODE_KQ); wall time per token (each
+    call is synchronous).  Weights as in the prefill step; x per call N(0,1)."""
+    import rocknpu_b200 as rk
+    plan = decode_plan()
+    slot = {"attn_q": 0, "attn_k": 1, "attn_v": 2, "attn_output": 0, "ffn_gate": 0, "ffn_up": 1, "ffn_down": 0}
+    group = {"attn_q": "qkv", "attn_k": "qkv", "attn_v": "qkv", "attn_output": "o", "ffn_gate": "gate_up",
+             "ffn_up": "gate_up", "ffn_down": "down"}
+    calls = []  # (entry, [(blocks, kind, n)], k, x, outs)
+    s = 7000
+    for layer, lcalls in enumerate(plan):
+        for call, members, k in lcalls:
+            ms = []
+            for name, kind, n in members:
+                short = name.split(".")[2]
+                blocks = weights[(layer, group[short])][slot[short]]
+                if blocks.size != n * (k // 256) * rk.BLOCK_BYTES[kind]:
+                    raise RuntimeError(f"decode plan member {name} does not match the prefill weights")
+                ms.append((blocks, kind, n))
+            x = rk.host_empty((k,))
+            x[...] = rk.synth_normal(s, k)
+            s += 1
+            calls.append((call, ms, k, x, [rk.host_empty((n,)) for _, _, n in ms]))
+    weight_bytes = sum(b.nbytes for _, ms, _, _, _ in calls for b, _, _ in ms)
+    int8_bytes = sum(n * k for _, ms, k, _, _ in calls for _, _, n in ms)
+    rows = sum(n for _, ms, _, _, _ in calls for _, _, n in ms)
+    hbm_gbs = load_peaks()[0]
+
+    def token(ctx):
+        for call, ms, k, x, outs in calls:
+            if call == "triple_m1":
+                (w1, k1, n1), (w2, k2, n2), (w3, k3, n3) = ms
+                st = ctx.matmul_q_triple_m1(w1, k1, n1, w2, k2, n2, w3, k3, n3, x, *outs, k)
+            elif call == "pair_m1":
+                (w1, k1, n1), (w2, k2, n2) = ms
+                st = ctx.matmul_q_pair_m1(w1, k1, n1, w2, k2, n2, x, outs[0], outs[1], k)
+            else:
+                w, kd, n = ms[0]
+                st = ctx.matmul_q(kd, w, x, outs[0], 1, k, n)
+            if st != 0:
+                raise RuntimeError(f"decode call {call} failed: {st}")
+
+    res = {"tokens": tokens, "calls_per_token": len(calls), "planned_by": "rocknpu_graph_plan, ROCKNPU_DECODE=npu",
+           "path": "rocknpu_matmul_q_triple/pair_f32_f32_m1 + rocknpu_matmul_q{4,6}_k_f32_f32 at m = 1, "
+                   "rocknpu_b200_host_alloc host buffers"}
+    for route, env in (("w8a8", None), ("kq", "1")):
+        old = os.environ.pop("ROCKNPU_B200_DECODE_KQ", None)
+        if env is not None:
+            os.environ["ROCKNPU_B200_DECODE_KQ"] = env
+        try:
+            ctx = rk.Context()  # the route is read when the context is created
+        finally:
+            os.environ.pop("ROCKNPU_B200_DECODE_KQ", None)
+            if old is not None:
+                os.environ["ROCKNPU_B200_DECODE_KQ"] = old
+        try:
+            for _ in range(max(1, warmup)):
+                token(ctx)  # the first token also builds the resident decode weights
+            t0 = time.perf_counter()
+            for _ in range(tokens):
+                token(ctx)
+            dt = (time.perf_counter() - t0) / tokens
+            resident = ctx.decode_cache_stats().resident_bytes
+        finally:
+            ctx.close()
+        # weight bytes one token streams on this route, and their time at the
+        # measured copy rate (the calls are host-round-trip bound well above it)
+        streamed = int8_bytes + 4 * rows if route == "w8a8" else weight_bytes
+        res[route] = {"tok_s": round(1.0 / dt, 1), "ms_per_token": round(dt * 1e3, 3),
+                      "us_per_call": round(dt * 1e6 / len(calls), 1), "resident_weight_bytes": int(resident),
+                      "weight_bytes_per_token": int(streamed),
+                      "hbm_floor_ms": round(streamed / (hbm_gbs * 1e9) * 1e3, 4)}
+    res["numerics"] = "w8a8: the reference's W8A8 bits; kq: f32 within 1e-3 of the exact product"
+    return res
 
 
 # Token rows of the CPU samples: the CPU path's cost is linear in the rows,
@@ -1128,6 +1238,7 @@ def main():
                     help="cfg5 output exchange at N > 1")
     ap.add_argument("--m-list", default=",".join(str(m) for m in CFG5_M))
     ap.add_argument("--no-check", action="store_true", help="cfg5 at N > 1: skip the in-run bit check")
+    ap.add_argument("--no-decode", action="store_true", help="skip the M=1 decode-token measurement")
     ap.add_argument("--no-cfg5", action="store_true",
                     help="default workload: skip the cfg5 GEMM/GEMV block (N=1) or the sharded block (N>1)")
     ap.add_argument("--f16", action="store_true", help="model workloads through the FP16 executor (one GPU)")

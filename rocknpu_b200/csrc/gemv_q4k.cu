@@ -119,6 +119,7 @@ __global__ void q4k_planes_kernel(const uint4* __restrict__ src, long long nbloc
 struct Q4Fmt {
     static constexpr int kCodeBytes = 128;    // qs
     static constexpr int kHeadBytes = 16;     // d, dmin, regrouped scales and mins
+    static constexpr bool kSplitFull = true;
     static constexpr int kBlocksPerStep = 8;  // 4 lanes per block
     static int sr_align(int) { return 1; }    // plane 2 is 16 bytes per block
     // lane-order x: per step 9 pieces x 32 lanes x 16 bytes

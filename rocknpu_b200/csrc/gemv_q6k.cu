@@ -80,6 +80,7 @@ __global__ void q6k_planes_kernel(const uint8_t* __restrict__ src, long long nbl
 struct Q6Fmt {
     static constexpr int kCodeBytes = 208;    // four 48-byte groups + regrouped scales
     static constexpr int kHeadBytes = 2;      // d
+    static constexpr bool kSplitFull = false;
     static constexpr int kBlocksPerStep = 8;  // 4 lanes per block
     // plane 2 holds 2 bytes per block: a stage's d range starts 16-byte
     // aligned when sr * nb is a multiple of 8
