@@ -42,3 +42,25 @@ def test_layer_plan_follows_the_q4_k_m_mix():
         qkv = plan[0][1]
         assert [kind for kind, _ in qkv] == [4, 4, 6]  # attn_v in Q6_K
         assert plan[3][1][0][0] == (6 if layer % 2 == 0 else 4)  # every other ffn_down in Q6_K
+
+
+def test_decode_plan_is_the_planner_m1_calls_on_the_prefill_weights():
+    """The bench's decode key replays rocknpu_graph_plan's M=1 calls with the
+    plugin's decode switch on: per layer the QKV triple (q, v, k), o, the
+    gate/up pair and down -- 88 calls per token -- and every member is a
+    prefill weight of the same kind and shape (the same resident bytes)."""
+    bench.set_model("tinyllama")
+    before = os.environ.get("ROCKNPU_DECODE")
+    plan = bench.decode_plan()
+    assert os.environ.get("ROCKNPU_DECODE") == before  # the switch is restored
+    assert len(plan) == 22 and sum(len(calls) for calls in plan) == 88
+    group = {"attn_q": ("qkv", 0), "attn_k": ("qkv", 1), "attn_v": ("qkv", 2), "attn_output": ("o", 0),
+             "ffn_gate": ("gate_up", 0), "ffn_up": ("gate_up", 1), "ffn_down": ("down", 0)}
+    for layer, calls in enumerate(plan):
+        assert [c for c, _, _ in calls] == ["triple_m1", "single", "pair_m1", "single"]
+        assert [name.split(".")[2] for name, _, _ in calls[0][1]] == ["attn_q", "attn_v", "attn_k"]
+        prefill = {name: (members, k) for name, members, k in bench.layer_plan(layer)}
+        for _, members, k in calls:
+            for name, kind, n in members:
+                call, slot = group[name.split(".")[2]]
+                assert prefill[call][0][slot] == (kind, n) and prefill[call][1] == k
