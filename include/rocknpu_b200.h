@@ -231,7 +231,11 @@ int rocknpu_b200_gemm_w8a8(const int8_t *a_i8, size_t ld_a, const float *a_scale
 
 /* K2 + K3 (+ K5 for m == 1) through the context's workspace: the whole
  * W8A8 MUL_MAT on resident f32 activations and resident prepared weights
- * (complete before the call: see rocknpu_b200_gemm_w8a8). */
+ * (complete before the call: see rocknpu_b200_gemm_w8a8).  A NULL `stream`
+ * queues the work on the context's own stream (not the legacy default
+ * stream); rocknpu_b200_context_check waits for that stream and returns the
+ * status word.  Device errors (a non-finite activation) go to the context's
+ * status word; `out` is unspecified when it is not 0. */
 int rocknpu_b200_matmul_w8a8(rocknpu_context *context, const float *a, const int8_t *w_i8, const float *w_scales,
                              float *out, size_t m, size_t k, size_t n, rocknpu_stream stream);
 

@@ -125,7 +125,10 @@ def gemv_kq(kind: int, layout: torch.Tensor, x: torch.Tensor, n: int, status: to
 
 
 def matmul_w8a8(ctx, a: torch.Tensor, w8: torch.Tensor, w_scales: torch.Tensor, out: torch.Tensor, stream=None):
-    """K2 + K3 (K5 at m == 1) through a context's workspace."""
+    """K2 + K3 (K5 at m == 1) through a context's workspace.  On torch's
+    default stream (handle 0, also what stream=None gives there) the work
+    runs on the context's own stream: rocknpu_b200_context_check (or a device
+    synchronisation) orders it before later reads of `out`."""
     m, k = a.shape
     n = w8.shape[0]
     _check(lib().rocknpu_b200_matmul_w8a8(ctx.handle, a.data_ptr(), w8.data_ptr(), w_scales.data_ptr(),
