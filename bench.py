@@ -50,6 +50,7 @@ The large cfg5 GEMMs do shard (the `shard` key above).
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -533,15 +534,33 @@ def run_ours(args, rank: int, world: int):
             members = layer_plan(key[0])[["qkv", "o", "gate_up", "down"].index(key[1])][1]
             h_outs[key] = [rk.host_empty((m, n)) for _, n in members]
 
+        # each call as (C-ABI function, arguments) with the buffers' addresses
+        # taken once (the arrays stay alive in weights / h_acts / h_outs), so
+        # the timed loop costs what a C caller's would plus one ctypes call
+        L = rk.lib()
+        qfn = {4: L.rocknpu_matmul_q4_k_f32_f32, 6: L.rocknpu_matmul_q6_k_f32_f32}
+        bound = []
+        for key, blocks in weights.items():
+            _, members, k = layer_plan(key[0])[["qkv", "o", "gate_up", "down"].index(key[1])]
+            a, os_ = h_acts[key], h_outs[key]
+            if len(members) > 1:
+                cnt = len(members)
+                arrs = ((ctypes.c_void_p * cnt)(*[b.ctypes.data for b in blocks]),
+                        (ctypes.c_size_t * cnt)(*[b.nbytes for b in blocks]),
+                        (ctypes.c_uint32 * cnt)(*[kd for kd, _ in members]),
+                        (ctypes.c_size_t * cnt)(*[n for _, n in members]),
+                        (ctypes.c_void_p * cnt)(*[o.ctypes.data for o in os_]))
+                bound.append((key, L.rocknpu_matmul_q_concat_f32_f32_mtile,
+                              (ctx.handle, cnt, arrs[0], arrs[1], arrs[2], arrs[3], a.ctypes.data, arrs[4], m, k),
+                              arrs))
+            else:
+                kd, n = members[0]
+                bound.append((key, qfn[kd], (ctx.handle, blocks[0].ctypes.data, blocks[0].nbytes, a.ctypes.data,
+                                             os_[0].ctypes.data, m, k, n), None))
+
         def e2e_step():
-            for key, blocks in weights.items():
-                _, members, k = layer_plan(key[0])[["qkv", "o", "gate_up", "down"].index(key[1])]
-                a = h_acts[key]
-                os_ = h_outs[key]
-                if len(members) > 1:
-                    st = ctx.matmul_q_concat(blocks, [kd for kd, _ in members], [n for _, n in members], a, os_, m, k)
-                else:
-                    st = ctx.matmul_q(members[0][0], blocks[0], a, os_[0], m, k, members[0][1])
+            for key, fn, args, _ in bound:
+                st = fn(*args)
                 if st != 0:
                     raise RuntimeError(f"C ABI call {key} failed: {st}")
 
@@ -678,17 +697,33 @@ def decode_block(weights, tokens, warmup):
     rows = sum(n for _, ms, _, _, _ in calls for _, _, n in ms)
     hbm_gbs = load_peaks()[0]
 
-    def token(ctx):
+    def bind(ctx):
+        # each call as (C-ABI function, its arguments) with the buffers'
+        # addresses taken once (the arrays stay alive in `calls`): the loop
+        # then costs what a C caller's would plus one ctypes call
+        L, h = rk.lib(), ctx.handle
+        fns = {4: L.rocknpu_matmul_q4_k_f32_f32, 6: L.rocknpu_matmul_q6_k_f32_f32}
+        bound = []
         for call, ms, k, x, outs in calls:
+            xa, oa = x.ctypes.data, [o.ctypes.data for o in outs]
             if call == "triple_m1":
-                (w1, k1, n1), (w2, k2, n2), (w3, k3, n3) = ms
-                st = ctx.matmul_q_triple_m1(w1, k1, n1, w2, k2, n2, w3, k3, n3, x, *outs, k)
+                args = [h]
+                for w, kd, n in ms:
+                    args += [w.ctypes.data, w.nbytes, kd, n]
+                bound.append((call, L.rocknpu_matmul_q_triple_f32_f32_m1, tuple(args + [xa] + oa + [k])))
             elif call == "pair_m1":
-                (w1, k1, n1), (w2, k2, n2) = ms
-                st = ctx.matmul_q_pair_m1(w1, k1, n1, w2, k2, n2, x, outs[0], outs[1], k)
+                args = [h]
+                for w, kd, n in ms:
+                    args += [w.ctypes.data, w.nbytes, kd, n]
+                bound.append((call, L.rocknpu_matmul_q_pair_f32_f32_m1, tuple(args + [xa] + oa + [k])))
             else:
                 w, kd, n = ms[0]
-                st = ctx.matmul_q(kd, w, x, outs[0], 1, k, n)
+                bound.append((call, fns[kd], (h, w.ctypes.data, w.nbytes, xa, oa[0], 1, k, n)))
+        return bound
+
+    def token(bound):
+        for call, fn, args in bound:
+            st = fn(*args)
             if st != 0:
                 raise RuntimeError(f"decode call {call} failed: {st}")
 
@@ -706,11 +741,12 @@ def decode_block(weights, tokens, warmup):
             if old is not None:
                 os.environ["ROCKNPU_B200_DECODE_KQ"] = old
         try:
+            bound = bind(ctx)
             for _ in range(max(1, warmup)):
-                token(ctx)  # the first token also builds the resident decode weights
+                token(bound)  # the first token also builds the resident decode weights
             t0 = time.perf_counter()
             for _ in range(tokens):
-                token(ctx)
+                token(bound)
             dt = (time.perf_counter() - t0) / tokens
             resident = ctx.decode_cache_stats().resident_bytes
         finally:
