@@ -187,18 +187,22 @@ struct DevBuf {
     }
 };
 
-// Page-locked host memory, grown like DevBuf; the owner makes sure no copy
-// that uses it is in flight when it grows or is released.
+// Page-locked host memory mapped into the device's address space (dptr: the
+// device's address of it), grown like DevBuf; the owner makes sure no copy or
+// kernel that uses it is in flight when it grows or is released.
 struct HostBuf {
     void* ptr = nullptr;
+    void* dptr = nullptr;
     size_t cap = 0;
     cudaError_t ensure(size_t bytes) {
         if (bytes <= cap) return cudaSuccess;
         release();
         const size_t want = round_up(bytes + bytes / 4, 64 << 10);
-        const cudaError_t e = cudaHostAlloc(&ptr, want, cudaHostAllocDefault);
+        cudaError_t e = cudaHostAlloc(&ptr, want, cudaHostAllocMapped);
+        if (e == cudaSuccess) e = cudaHostGetDevicePointer(&dptr, ptr, 0);
         if (e != cudaSuccess) {
-            ptr = nullptr;
+            if (ptr) cudaFreeHost(ptr);
+            ptr = dptr = nullptr;
             return e;
         }
         cap = want;
@@ -206,7 +210,7 @@ struct HostBuf {
     }
     void release() {
         if (ptr) cudaFreeHost(ptr);
-        ptr = nullptr;
+        ptr = dptr = nullptr;
         cap = 0;
     }
     template <class T>
@@ -552,23 +556,33 @@ void zero_copy_mode(bool* in, bool* out) {
 // three operations (copy, kernels, copy) where the general path has seven.
 // On an error the caller's outputs are untouched; a non-finite x is
 // INVALID_ARGUMENT, as on the general path.
+//
+// host_out: the kernels write y and the status word straight into the
+// page-locked block through its device mapping (plain stores; see
+// launch_gemv_w8a8_x), so only x is copied and there is no output copy.
 template <class Launch>
-int m1_call(Ctx* c, const float* a, size_t k, const OutSeg* segs, size_t nseg, bool overlap, Launch&& launch) {
+int m1_call(Ctx* c, const float* a, size_t k, const OutSeg* segs, size_t nseg, bool overlap, bool host_out,
+            Launch&& launch) {
     size_t total = 0;
     for (size_t i = 0; i < nseg; ++i) total += segs[i].n;
     const size_t y_bytes = round_up(total * sizeof(float), 16);
     const size_t bytes = y_bytes + 16 + k * sizeof(float);
     if (c->m1_dev.ensure(bytes) != cudaSuccess || c->m1_host.ensure(bytes) != cudaSuccess) return kExecError;
     uint8_t* hb = c->m1_host.as<uint8_t>();
+    uint8_t* hd = static_cast<uint8_t*>(c->m1_host.dptr);
     uint8_t* db = c->m1_dev.as<uint8_t>();
     int* h_st = reinterpret_cast<int*>(hb + y_bytes);
     std::memset(h_st, 0, 16);
     std::memcpy(hb + y_bytes + 16, a, k * sizeof(float));
-    if (cudaMemcpyAsync(db + y_bytes, hb + y_bytes, 16 + k * sizeof(float), cudaMemcpyHostToDevice, c->stream))
+    const size_t in_off = host_out ? y_bytes + 16 : y_bytes;  // the status word travels only without host_out
+    if (cudaMemcpyAsync(db + in_off, hb + in_off, bytes - in_off, cudaMemcpyHostToDevice, c->stream))
         return kExecError;
-    if (launch(reinterpret_cast<const float*>(db + y_bytes + 16), reinterpret_cast<float*>(db),
-               reinterpret_cast<int*>(db + y_bytes)) != cudaSuccess)
-        return kExecError;
+    const cudaError_t le =
+        host_out ? launch(reinterpret_cast<const float*>(db + y_bytes + 16), reinterpret_cast<float*>(hd),
+                          reinterpret_cast<int*>(hd + y_bytes))
+                 : launch(reinterpret_cast<const float*>(db + y_bytes + 16), reinterpret_cast<float*>(db),
+                          reinterpret_cast<int*>(db + y_bytes));
+    if (le != cudaSuccess) return kExecError;
     if (overlap && c->overlap) {
         // one-shot host work while the GPU runs (take_overlap, L:264-273)
         rocknpu_overlap_fn fn = c->overlap;
@@ -577,7 +591,8 @@ int m1_call(Ctx* c, const float* a, size_t k, const OutSeg* segs, size_t nseg, b
         c->overlap_user = nullptr;
         fn(user);
     }
-    if (cudaMemcpyAsync(hb, db, y_bytes + 16, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess) return kExecError;
+    if (!host_out && cudaMemcpyAsync(hb, db, y_bytes + 16, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
+        return kExecError;
     if (wait_stream(c->stream) != cudaSuccess) return kExecError;
     const int s = *h_st;
     if (s != rk::kErrNone) return s == rk::kErrNonFinite ? kInvalid : kExecError;
@@ -605,11 +620,12 @@ int run_w8a8(Ctx* c, const PreparedW8& pw, const float* host_a, size_t m, size_t
     const size_t total_n = pw.n;
     if (m == 1 && k % 16 == 0 && !dev_a) {
         // K2 + K5 fused into one launch (the row quantiser's bits)
-        return m1_call(c, host_a, k, segs, nseg, m1_overlap, [&](const float* x, float* y, int* err) {
-            rk::launch_gemv_w8a8_x(pw.w, pw.scales, x, static_cast<int>(k), static_cast<int>(total_n), y, err,
-                                   c->stream);
-            return cudaGetLastError();
-        });
+        return m1_call(c, host_a, k, segs, nseg, m1_overlap, /*host_out=*/true,
+                       [&](const float* x, float* y, int* err) {
+                           rk::launch_gemv_w8a8_x(pw.w, pw.scales, x, static_cast<int>(k), static_cast<int>(total_n),
+                                                  y, err, c->stream, /*host_out=*/true);
+                           return cudaGetLastError();
+                       });
     }
     if ((!dev_a && c->a_f32.ensure(m * k * sizeof(float))) || c->a_i8.ensure(m * ld8) ||
         c->a_scale.ensure(m * sizeof(float)) || c->out_f32.ensure(m * total_n * sizeof(float)))
@@ -898,7 +914,7 @@ int decode_kq_m1(Ctx* c, const KeyList& keys, const Member* members, size_t coun
         c->kq.emplace(keys[i], p[i]);
     }
     if (!hit) c->m1_shapes.insert({k, total});
-    const int st = m1_call(c, a, k, segs, count, true, [&](const float* x, float* y, int* err) {
+    const int st = m1_call(c, a, k, segs, count, true, /*host_out=*/false, [&](const float* x, float* y, int* err) {
         for (size_t i = 0; i < count; ++i) {
             const int e = rk::launch_gemv_kq(p[i]->kind, p[i]->layout, static_cast<int>(k), static_cast<int>(p[i]->n),
                                              x, y, err, c->stream);

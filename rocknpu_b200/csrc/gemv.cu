@@ -23,14 +23,14 @@ __device__ __forceinline__ int4 ld_stream(const int4* p) {
     return v;
 }
 
-// Rows of one CTA against the quantised activation staged in shared memory.
-__device__ __forceinline__ void gemv_rows(const int4* sa, const int8_t* __restrict__ w,
-                                          const float* __restrict__ w_scale, float a_scale, int k, int n,
-                                          float* __restrict__ out) {
+// The warp's row of this CTA against the quantised activation staged in
+// shared memory: the rescaled result, in every lane (0 for a row past n).
+__device__ __forceinline__ float gemv_row(const int4* sa, const int8_t* __restrict__ w,
+                                          const float* __restrict__ w_scale, float a_scale, int k, int n) {
     const int chunks = k >> 4;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * kRowsPerCta + warp;
-    if (row >= n) return;
+    if (row >= n) return 0.0f;
     const int4* wr = reinterpret_cast<const int4*>(w + static_cast<size_t>(row) * k);
     int acc = 0;
     int i = lane;
@@ -50,7 +50,7 @@ __device__ __forceinline__ void gemv_rows(const int4* sa, const int8_t* __restri
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) out[row] = __fmul_rn(__fmul_rn(__int2float_rn(acc), a_scale), w_scale[row]);
+    return __fmul_rn(__fmul_rn(__int2float_rn(acc), a_scale), w_scale[row]);
 }
 
 __global__ void __launch_bounds__(kGemvThreads) gemv_w8a8_kernel(const int8_t* __restrict__ w,
@@ -62,7 +62,9 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_w8a8_kernel(const int8_t* _
     const int chunks = k >> 4;
     for (int i = threadIdx.x; i < chunks; i += kGemvThreads) sa[i] = reinterpret_cast<const int4*>(a8)[i];
     __syncthreads();
-    gemv_rows(sa, w, w_scale, *a_scale, k, n, out);
+    const float v = gemv_row(sa, w, w_scale, *a_scale, k, n);
+    const int row = blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
+    if ((threadIdx.x & 31) == 0 && row < n) out[row] = v;
 }
 
 // K2 + K5 in one launch for M=1: every CTA quantises the f32 activation x
@@ -71,7 +73,11 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_w8a8_kernel(const int8_t* _
 // per-value rounding, so the same bits -- then runs the rows above.  The
 // repeated work per CTA is one 4k-byte read of x (L2-resident after the
 // first CTAs) and a block reduction.  A non-finite x sets kErrNonFinite and
-// no output is written.
+// no output is written.  HostOut: `out` and `err` are page-locked host memory
+// mapped into the device: a CTA's 8 results leave as one 32-byte store, and
+// the error is a plain store (every writer stores the same value; atomics to
+// host memory need PCIe atomics).
+template <bool HostOut>
 __global__ void __launch_bounds__(kGemvThreads) gemv_w8a8_x_kernel(const int8_t* __restrict__ w,
                                                                     const float* __restrict__ w_scale,
                                                                     const float* __restrict__ x, int k, int n,
@@ -88,7 +94,12 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_w8a8_x_kernel(const int8_t*
         amax = fmaxf(fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y))), fmaxf(fabsf(v.z), fabsf(v.w)));
     }
     if (__syncthreads_or(!finite)) {
-        if (threadIdx.x == 0) atomicExch(err, kErrNonFinite);
+        if (threadIdx.x == 0) {
+            if constexpr (HostOut)
+                *reinterpret_cast<volatile int*>(err) = kErrNonFinite;
+            else
+                atomicExch(err, kErrNonFinite);
+        }
         return;
     }
     amax = warp_max(amax);
@@ -101,7 +112,17 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_w8a8_x_kernel(const int8_t*
     uint32_t* sa32 = reinterpret_cast<uint32_t*>(sa);
     for (int i = threadIdx.x; i < k4; i += kGemvThreads) sa32[i] = quant_pack4(__ldg(x4 + i), scale, inv);
     __syncthreads();
-    gemv_rows(sa, w, w_scale, scale, k, n, out);
+    const float v = gemv_row(sa, w, w_scale, scale, k, n);
+    if constexpr (HostOut) {
+        __shared__ float res[kRowsPerCta];
+        if ((threadIdx.x & 31) == 0) res[threadIdx.x >> 5] = v;
+        __syncthreads();
+        const int r = blockIdx.x * kRowsPerCta + threadIdx.x;
+        if (threadIdx.x < kRowsPerCta && r < n) out[r] = res[threadIdx.x];
+    } else {
+        const int row = blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
+        if ((threadIdx.x & 31) == 0 && row < n) out[row] = v;
+    }
 }
 
 }  // namespace
@@ -116,12 +137,11 @@ void launch_gemv_w8a8(const int8_t* w, const float* w_scale, const int8_t* a8, c
 }
 
 void launch_gemv_w8a8_x(const int8_t* w, const float* w_scale, const float* x, int k, int n, float* out, int* err,
-                        cudaStream_t s) {
+                        cudaStream_t s, bool host_out) {
     const size_t smem = static_cast<size_t>(k);
-    if (smem > 48 * 1024)
-        cudaFuncSetAttribute(gemv_w8a8_x_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    gemv_w8a8_x_kernel<<<(n + kRowsPerCta - 1) / kRowsPerCta, kGemvThreads, smem, s>>>(w, w_scale, x, k, n, out,
-                                                                                       err);
+    auto kern = host_out ? gemv_w8a8_x_kernel<true> : gemv_w8a8_x_kernel<false>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    kern<<<(n + kRowsPerCta - 1) / kRowsPerCta, kGemvThreads, smem, s>>>(w, w_scale, x, k, n, out, err);
 }
 
 }  // namespace rk

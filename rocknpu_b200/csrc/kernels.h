@@ -106,8 +106,10 @@ void launch_gemv_w8a8(const int8_t* w, const float* w_scale, const int8_t* a8, c
                       float* out, cudaStream_t s);
 // K2 + K5 fused for M=1: x f32 (16-byte aligned, k % 16 == 0) quantised per
 // CTA with the row quantiser's bits, then the GEMV; kErrNonFinite into *err.
+// host_out: out and err are mapped page-locked host memory (written with
+// plain stores, the results 32 bytes per CTA).
 void launch_gemv_w8a8_x(const int8_t* w, const float* w_scale, const float* x, int k, int n, float* out, int* err,
-                        cudaStream_t s);
+                        cudaStream_t s, bool host_out = false);
 
 // K5b: M=1 GEMV straight from K-quant blocks (gemv_kq.cu dispatches to
 // gemv_q4k.cu / gemv_q6k.cu).  The decode layout of a Q4_K weight is two
