@@ -914,10 +914,10 @@ int decode_kq_m1(Ctx* c, const KeyList& keys, const Member* members, size_t coun
         c->kq.emplace(keys[i], p[i]);
     }
     if (!hit) c->m1_shapes.insert({k, total});
-    const int st = m1_call(c, a, k, segs, count, true, /*host_out=*/false, [&](const float* x, float* y, int* err) {
+    const int st = m1_call(c, a, k, segs, count, true, /*host_out=*/true, [&](const float* x, float* y, int* err) {
         for (size_t i = 0; i < count; ++i) {
             const int e = rk::launch_gemv_kq(p[i]->kind, p[i]->layout, static_cast<int>(k), static_cast<int>(p[i]->n),
-                                             x, y, err, c->stream);
+                                             x, y, err, c->stream, /*host_out=*/true);
             if (e != cudaSuccess) return static_cast<cudaError_t>(e);
             y += p[i]->n;
         }

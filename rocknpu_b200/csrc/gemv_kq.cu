@@ -44,10 +44,10 @@ int launch_kq_layout(int kind, const uint8_t* blocks, int k, int n, uint8_t* lay
 // k up to 24576 (the stage ring and the lane-order x fit shared memory well
 // beyond that, but the documented limit stays what the tests cover).
 int launch_gemv_kq(int kind, const uint8_t* layout, int k, int n, const float* x, float* y, int* err,
-                   cudaStream_t s) {
+                   cudaStream_t s, bool host_out) {
     if (k > 24576) return cudaErrorInvalidValue;
-    if (kind == kQ4K) return launch_gemv_q4k(layout, k, n, x, y, err, s);
-    if (kind == kQ6K) return launch_gemv_q6k(layout, k, n, x, y, err, s);
+    if (kind == kQ4K) return launch_gemv_q4k(layout, k, n, x, y, err, s, host_out);
+    if (kind == kQ6K) return launch_gemv_q6k(layout, k, n, x, y, err, s, host_out);
     return cudaErrorInvalidValue;
 }
 

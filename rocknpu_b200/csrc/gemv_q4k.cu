@@ -142,7 +142,7 @@ struct Q4Fmt {
             for (int i = 0; i < 16; ++i)
                 m = fmaxf(m, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
             const bool finite = isfinite(m);
-            if (!finite) atomicCAS(p.err, 0, kErrNonFinite);
+            if (!finite) kq::set_err(p, kErrNonFinite);
             const float inv = (finite && m > 0.f) ? 32767.f / m : 0.f;
             const float scale = (finite && m > 0.f) ? m / 32767.f : 0.f;
             uint32_t packed[32];
@@ -239,12 +239,13 @@ int launch_q4k_layout(const uint8_t* blocks, int k, int n, uint8_t* layout, cuda
     return cudaGetLastError();
 }
 
-int launch_gemv_q4k(const uint8_t* layout, int k, int n, const float* x, float* y, int* err, cudaStream_t s) {
+int launch_gemv_q4k(const uint8_t* layout, int k, int n, const float* x, float* y, int* err, cudaStream_t s,
+                    bool host_out) {
     if (k <= 0 || k % 256 != 0 || n <= 0 || !layout || !x || !y || !err) return cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(layout) % 16) || (reinterpret_cast<uintptr_t>(x) % 16))
         return cudaErrorInvalidValue;
     const size_t nb = static_cast<size_t>(k / 256);
-    return kq::launch_stage<Q4Fmt>(layout, layout + static_cast<size_t>(n) * nb * 128, k, n, x, y, err, s);
+    return kq::launch_stage<Q4Fmt>(layout, layout + static_cast<size_t>(n) * nb * 128, k, n, x, y, err, s, host_out);
 }
 
 }  // namespace rk

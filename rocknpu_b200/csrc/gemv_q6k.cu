@@ -107,7 +107,7 @@ struct Q6Fmt {
             for (int i = 0; i < 8; ++i)
                 m = fmaxf(m, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
             const bool finite = isfinite(m);
-            if (!finite) atomicCAS(p.err, 0, kErrNonFinite);
+            if (!finite) kq::set_err(p, kErrNonFinite);
             const float inv = (finite && m > 0.f) ? 32767.f / m : 0.f;
             const float scale = (finite && m > 0.f) ? m / 32767.f : 0.f;
             uint32_t packed[16];
@@ -220,12 +220,13 @@ int launch_q6k_layout(const uint8_t* blocks, int k, int n, uint8_t* layout, cuda
     return e != cudaSuccess ? e : cudaGetLastError();
 }
 
-int launch_gemv_q6k(const uint8_t* layout, int k, int n, const float* x, float* y, int* err, cudaStream_t s) {
+int launch_gemv_q6k(const uint8_t* layout, int k, int n, const float* x, float* y, int* err, cudaStream_t s,
+                    bool host_out) {
     if (k <= 0 || k % 256 != 0 || n <= 0 || !layout || !x || !y || !err) return cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(layout) % 16) || (reinterpret_cast<uintptr_t>(x) % 16))
         return cudaErrorInvalidValue;
     const size_t nb = static_cast<size_t>(k / 256);
-    return kq::launch_stage<Q6Fmt>(layout, layout + static_cast<size_t>(n) * nb * 208, k, n, x, y, err, s);
+    return kq::launch_stage<Q6Fmt>(layout, layout + static_cast<size_t>(n) * nb * 208, k, n, x, y, err, s, host_out);
 }
 
 }  // namespace rk

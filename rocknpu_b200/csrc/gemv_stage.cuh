@@ -57,7 +57,19 @@ struct StageParams {
     int k, n, nb;
     int steps;  // steps per row: ceil(nb / F::kBlocksPerStep)
     int sr;     // rows per stage (a multiple of the rows per unit)
+    int err_plain;  // err (and y) are mapped host memory: errors by plain store
 };
+
+// Record an error code: in device memory the first error wins (atomic); a
+// status word in mapped host memory takes a plain store (atomics to host
+// memory need PCIe atomic operations), so there a later error code may
+// replace an earlier one -- either way the word is non-zero.
+__device__ __forceinline__ void set_err(const StageParams& p, int code) {
+    if (p.err_plain)
+        *reinterpret_cast<volatile int*>(p.err) = code;
+    else
+        atomicCAS(p.err, 0, code);
+}
 
 // acc + X0 * b0 + X1 * b1 + X2 * b2 + X3 * b3: the 4 unsigned byte codes of
 // `codes` against the signed 16-bit X packed two per word in x01, x23.
@@ -208,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 2) stage_kernel(const StageParams p)
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok || abort_all) {
                 if (lane == 0 && !abort_all) {
-                    atomicCAS(p.err, 0, kErrTimeoutEmpty);
+                    set_err(p, kErrTimeoutEmpty);
                     abort_all = 1;
                 }
                 break;
@@ -239,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 2) stage_kernel(const StageParams p)
             const int sl = k % S;
             if (!mbar_wait(&full[sl], (k / S) & 1)) {
                 if (!abort_all) {
-                    atomicCAS(p.err, 0, kErrTimeoutFull);
+                    set_err(p, kErrTimeoutFull);
                     abort_all = 1;
                 }
                 break;
@@ -288,8 +300,9 @@ __global__ void __launch_bounds__(kThreads, 2) stage_kernel(const StageParams p)
 // do not depend on it.  F::x_bytes and the ring must fit 200 KB.
 template <class F>
 int launch_stage(const uint8_t* codes, const uint8_t* heads, int k, int n, const float* x, float* y, int* err,
-                 cudaStream_t s) {
+                 cudaStream_t s, bool host_out = false) {
     StageParams p{};
+    p.err_plain = host_out ? 1 : 0;
     p.k = k;
     p.n = n;
     p.nb = k / 256;

@@ -120,14 +120,16 @@ void launch_gemv_w8a8_x(const int8_t* w, const float* w_scale, const float* x, i
 // values [n][k/256] and 16 bytes of padding.
 size_t kq_layout_bytes(int kind, size_t k, size_t n);
 int launch_q4k_layout(const uint8_t* blocks, int k, int n, uint8_t* layout, cudaStream_t s);
-int launch_gemv_q4k(const uint8_t* layout, int k, int n, const float* x, float* y, int* err, cudaStream_t s);
+int launch_gemv_q4k(const uint8_t* layout, int k, int n, const float* x, float* y, int* err, cudaStream_t s,
+                    bool host_out = false);
 int launch_q6k_layout(const uint8_t* blocks, int k, int n, uint8_t* layout, cudaStream_t s);
-int launch_gemv_q6k(const uint8_t* layout, int k, int n, const float* x, float* y, int* err, cudaStream_t s);
+int launch_gemv_q6k(const uint8_t* layout, int k, int n, const float* x, float* y, int* err, cudaStream_t s,
+                    bool host_out = false);
 int launch_kq_layout(int kind, const uint8_t* blocks, int k, int n, uint8_t* layout, cudaStream_t s);
 // y[n] = dequant(W) . x in f32; layout and x 16-byte aligned, k % 256 == 0.
 // Returns a cudaError_t value.
 int launch_gemv_kq(int kind, const uint8_t* layout, int k, int n, const float* x, float* y, int* err,
-                   cudaStream_t s);
+                   cudaStream_t s, bool host_out = false);
 
 // HILO two-part activations: residual rows res = x - dequant(quant(x)) of
 // each f32 row (non-finite -> *err), and the elementwise sum of the two
