@@ -313,9 +313,9 @@ struct RockNpuContext {
     std::map<KeyList, W8Ptr> decode_groups;
     // Opt-in K5b decode route (ROCKNPU_B200_DECODE_KQ at creation): M=1
     // Q4_K / Q6_K members are served from decode layouts of their K-quant
-    // bytes, one cached layout per member key.
+    // bytes, one cached layout per same-kind group of a call's members.
     bool decode_kq = false;
-    std::map<Key, KqPtr> kq;
+    std::map<KeyList, KqPtr> kq;  // one layout per same-kind group of a call's members
     // FP16 executor weights and the FP16 route's dequantised weights.
     std::map<Key, F16Ptr> f16;
 
@@ -858,20 +858,32 @@ int q_prompt_f16(Ctx* c, int kind, const uint8_t* w, size_t bytes, const float* 
     return run_f16(c, *p, a, m, k, out, dev_a, keep);
 }
 
-// One member's K5b decode layout from its K-quant bytes (staged through
-// c->staging, repacked by rk::launch_kq_layout).
-int build_kq(Ctx* c, const Member& mb, size_t k, KqPtr& out) {
+// One K5b decode layout for a group of same-kind members concatenated along
+// N, from their K-quant bytes (staged through c->staging, repacked by
+// rk::launch_kq_layout).
+int build_kq(Ctx* c, const Member* const* group, size_t count, size_t k, KqPtr& out) {
     auto p = std::make_shared<PreparedKq>();
-    p->kind = mb.kind;
-    p->n = mb.n;
+    p->kind = group[0]->kind;
     p->k = k;
-    p->len = rk::kq_layout_bytes(mb.kind, k, mb.n);
+    size_t bytes = 0;
+    for (size_t i = 0; i < count; ++i) {
+        p->n += group[i]->n;
+        bytes += group[i]->bytes;
+    }
+    p->len = rk::kq_layout_bytes(p->kind, k, p->n);
     if (p->len == 0) return kInvalid;
     if (cudaMalloc(&p->layout, p->len) != cudaSuccess) return kExecError;
-    if (c->staging.ensure(mb.bytes) != cudaSuccess) return kExecError;
-    if (cudaMemcpyAsync(c->staging.ptr, mb.host, mb.bytes, cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
-        return kExecError;
-    if (rk::launch_kq_layout(mb.kind, c->staging.as<uint8_t>(), static_cast<int>(k), static_cast<int>(mb.n),
+    if (c->staging.ensure(bytes) != cudaSuccess) return kExecError;
+    // the members' blocks back to back: the blocks of the group's rows in order
+    // (each member's bytes are a multiple of the 144- or 210-byte block)
+    size_t off = 0;
+    for (size_t i = 0; i < count; ++i) {
+        if (cudaMemcpyAsync(c->staging.as<uint8_t>() + off, group[i]->host, group[i]->bytes, cudaMemcpyHostToDevice,
+                            c->stream) != cudaSuccess)
+            return kExecError;
+        off += group[i]->bytes;
+    }
+    if (rk::launch_kq_layout(p->kind, c->staging.as<uint8_t>(), static_cast<int>(k), static_cast<int>(p->n),
                              p->layout, c->stream) != cudaSuccess)
         return kExecError;
     const int st = cuda_status(wait_stream(c->stream));
@@ -894,32 +906,54 @@ bool kq_route(const Ctx* c, const Member* members, size_t count, size_t k) {
 // per weight for Q4_K, 0.82 for Q6_K, against 1 B of int8 rows) and returns
 // f32 results within 1e-3 of the exact product of the dequantised weights
 // and x, instead of the W8A8 route's bits.  Cache statistics count a call as
-// a hit when every member's layout was resident.
+// a hit when every group's layout was resident.
 int decode_kq_m1(Ctx* c, const KeyList& keys, const Member* members, size_t count, const float* a, OutSeg* segs,
                  size_t k) {
     const uint64_t t0 = now_ns();
+    // members grouped by kind (in order of first appearance, keeping their
+    // order inside a group): one layout and one GEMV launch per group, the
+    // outputs in group order
+    int order[4], ngroups = 0, gstart[5];
+    size_t n_order = 0;
+    for (size_t i = 0; i < count; ++i) {
+        bool seen = false;
+        for (size_t j = 0; j < i; ++j) seen = seen || members[j].kind == members[i].kind;
+        if (seen) continue;
+        gstart[ngroups++] = static_cast<int>(n_order);
+        for (size_t j = i; j < count; ++j)
+            if (members[j].kind == members[i].kind) order[n_order++] = static_cast<int>(j);
+    }
+    gstart[ngroups] = static_cast<int>(n_order);
     KqPtr p[4];
     bool hit = true;
     size_t total = 0;
-    for (size_t i = 0; i < count; ++i) {
-        total += members[i].n;
-        auto it = c->kq.find(keys[i]);
+    for (int g = 0; g < ngroups; ++g) {
+        KeyList gkeys;
+        const Member* gm[4];
+        for (int t = gstart[g]; t < gstart[g + 1]; ++t) {
+            gkeys.push_back(keys[order[t]]);
+            gm[t - gstart[g]] = &members[order[t]];
+            total += members[order[t]].n;
+        }
+        auto it = c->kq.find(gkeys);
         if (it != c->kq.end()) {
-            p[i] = it->second;
+            p[g] = it->second;
             continue;
         }
         hit = false;
-        const int st = build_kq(c, members[i], k, p[i]);
+        const int st = build_kq(c, gm, static_cast<size_t>(gstart[g + 1] - gstart[g]), k, p[g]);
         if (st != kOk) return st;
-        c->kq.emplace(keys[i], p[i]);
+        c->kq.emplace(gkeys, p[g]);
     }
     if (!hit) c->m1_shapes.insert({k, total});
-    const int st = m1_call(c, a, k, segs, count, true, /*host_out=*/true, [&](const float* x, float* y, int* err) {
-        for (size_t i = 0; i < count; ++i) {
-            const int e = rk::launch_gemv_kq(p[i]->kind, p[i]->layout, static_cast<int>(k), static_cast<int>(p[i]->n),
+    OutSeg osegs[4];
+    for (size_t t = 0; t < n_order; ++t) osegs[t] = segs[order[t]];
+    const int st = m1_call(c, a, k, osegs, count, true, /*host_out=*/true, [&](const float* x, float* y, int* err) {
+        for (int g = 0; g < ngroups; ++g) {
+            const int e = rk::launch_gemv_kq(p[g]->kind, p[g]->layout, static_cast<int>(k), static_cast<int>(p[g]->n),
                                              x, y, err, c->stream, /*host_out=*/true);
             if (e != cudaSuccess) return static_cast<cudaError_t>(e);
-            y += p[i]->n;
+            y += p[g]->n;
         }
         return cudaSuccess;
     });

@@ -98,14 +98,29 @@ def test_pair_m1(kq_ctx, kinds):
     _check(o1, kinds[0], w1, x, n)
     _check(o2, kinds[1], w2, x, n)
     s = kq_ctx.decode_cache_stats()
-    assert s.misses == 1 and s.entries == 2  # one layout per member
-    assert s.resident_bytes == _layout_bytes(kinds[0], k, n) + _layout_bytes(kinds[1], k, n)
-    # a member already resident from the pair is reused by a single call
+    # one layout (and one GEMV launch) per same-kind group of the members
+    if kinds[0] == kinds[1]:
+        assert s.misses == 1 and s.entries == 1
+        assert s.resident_bytes == _layout_bytes(kinds[0], k, 2 * n)
+    else:
+        assert s.misses == 1 and s.entries == 2
+        assert s.resident_bytes == _layout_bytes(kinds[0], k, n) + _layout_bytes(kinds[1], k, n)
+    p1, p2 = o1.copy(), o2.copy()
+    assert kq_ctx.matmul_q_pair_m1(w1, kinds[0], n, w2, kinds[1], n, x, o1, o2, k) == 0
+    assert np.array_equal(_bits(o1), _bits(p1)) and np.array_equal(_bits(o2), _bits(p2))  # deterministic
+    s2 = kq_ctx.decode_cache_stats()
+    assert s2.hits == s.hits + 1 and s2.entries == s.entries
+    # a single call on one member: its own group, which a mixed-kind pair
+    # already holds (a hit) and a same-kind pair does not (a new layout)
     y = np.empty(n, np.float32)
     assert kq_ctx.matmul_q(kinds[0], w1, x, y, 1, k, n) == 0
-    assert np.array_equal(_bits(y), _bits(o1))
-    s2 = kq_ctx.decode_cache_stats()
-    assert s2.hits == s.hits + 1 and s2.entries == 2
+    _check(y, kinds[0], w1, x, n)
+    s3 = kq_ctx.decode_cache_stats()
+    if kinds[0] == kinds[1]:
+        assert s3.misses == s2.misses + 1 and s3.entries == s2.entries + 1
+    else:
+        assert s3.hits == s2.hits + 1 and s3.entries == s2.entries
+        assert np.array_equal(_bits(y), _bits(o1))
 
 
 def test_triple_m1(kq_ctx):
@@ -118,6 +133,9 @@ def test_triple_m1(kq_ctx):
                                      *outs, k) == 0
     for o, w, kd, n in zip(outs, ws, kinds, ns):
         _check(o, kd, w, x, n)
+    # q and k (Q4_K) share a layout, v (Q6_K) has its own
+    s = kq_ctx.decode_cache_stats()
+    assert s.entries == 2 and s.resident_bytes == _layout_bytes(4, k, 2048 + 256) + _layout_bytes(6, k, 256)
 
 
 def test_non_finite_x_is_invalid_and_context_recovers(kq_ctx):
