@@ -200,7 +200,9 @@ int rocknpu_b200_status_code(int device_status);
 
 /* K1: Q4_K/Q5_K/Q6_K rows (kind 4/5/6, n rows of k values, k % 256 == 0) ->
  * int8 rows w_i8[n][k] + scales[n], bit-identical to the reference's
- * prepare_q*_k_w8a8 (capi/src/lib.rs:711-757, 974-994). */
+ * prepare_q*_k_w8a8 (capi/src/lib.rs:711-757, 974-994).  `blocks` must be
+ * 4-byte aligned (INVALID_ARGUMENT otherwise); Q4_K blocks at a 16-byte
+ * boundary take the faster one-thread-per-sub-block kernel. */
 int rocknpu_b200_prepare_w8(uint32_t kind, const uint8_t *blocks, size_t k, size_t n, int8_t *w_i8, float *scales,
                             int *status, rocknpu_stream stream);
 

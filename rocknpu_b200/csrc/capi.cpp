@@ -1584,8 +1584,8 @@ int rocknpu_b200_context_check(rocknpu_context* context) {
 int rocknpu_b200_prepare_w8(uint32_t kind, const uint8_t* blocks, size_t k, size_t n, int8_t* w_i8, float* scales,
                             int* status, rocknpu_stream stream) {
     if ((kind != 4 && kind != 5 && kind != 6) || !blocks || !w_i8 || !scales || !status || k == 0 || n == 0 ||
-        k % 256 != 0 || k > 56 * 1024 || n > 0x7fffffff)
-        return kInvalid;
+        k % 256 != 0 || k > 56 * 1024 || n > 0x7fffffff || reinterpret_cast<uintptr_t>(blocks) % 4 != 0)
+        return kInvalid;  // the kernels read the blocks in 4-byte (or wider) words
     rk::launch_prep_w8(static_cast<int>(kind), blocks, static_cast<int>(k), static_cast<int>(n), w_i8, scales, status,
                        static_cast<cudaStream_t>(stream));
     return cuda_status(cudaGetLastError());

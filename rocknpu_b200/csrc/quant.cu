@@ -231,6 +231,119 @@ __global__ void __launch_bounds__(kRowThreads) prep_w8_reg_kernel(const uint8_t*
     if (threadIdx.x == 0) scales[row] = scale;
 }
 
+// K1 for Q4_K with one thread per 32-value sub-block (8 per superblock; the
+// blocks 16-byte aligned).  A sub-block's values are v(q) = (d*sc)*q - dmin*m
+// over its 4-bit codes q, each step rounded as in dequant8, so v is monotonic
+// in q (rounding keeps order) and |v| over the sub-block peaks at its smallest
+// or largest code: the row's absmax, and whether every value is finite, come
+// from a byte-wise min / max of the codes and two values -- the same absmax as
+// taking every value.  Once the row scale is known, the sub-block's 16
+// possible values are quantised (quant_value: the per-value arithmetic of the
+// other paths) into a 16-byte table, and every 4 codes become their 4 int8
+// bytes through two byte permutes and a select on the code's top bit: the
+// same bytes as quantising each value.
+__device__ __forceinline__ void q4k_sub(const uint8_t* src, int t, float& d1, float& m1, uint4& c0, uint4& c1,
+                                        int& shift) {
+    const uint8_t* blk = src + static_cast<size_t>(t >> 3) * 144;
+    const int j = t & 7;
+    const uint32_t dd = ld32(blk);
+    const uint32_t s[3] = {ld32(blk + 4), ld32(blk + 8), ld32(blk + 12)};
+    int sc, mn;
+    scale_min_k4(j, s, sc, mn);
+    d1 = __fmul_rn(half_bits_to_float(dd), static_cast<float>(sc));
+    m1 = __fmul_rn(half_bits_to_float(dd >> 16), static_cast<float>(mn));
+    // sub-block j: the low (even j) or high (odd j) nibbles of qs[32 (j/2) ..]
+    const uint4* q = reinterpret_cast<const uint4*>(blk + 16 + 32 * (j >> 1));
+    c0 = q[0];
+    c1 = q[1];
+    shift = 4 * (j & 1);
+}
+
+__device__ __forceinline__ float q4k_value(float d1, float m1, uint32_t q) {
+    return __fsub_rn(__fmul_rn(d1, small_uint_to_float(q)), m1);
+}
+
+// int8 bytes of 4 codes (one per byte, 0..15) from the 16-byte table t[0..3].
+__device__ __forceinline__ uint32_t q4k_lookup4(uint32_t codes, const uint32_t (&t)[4]) {
+    const uint32_t lo3 = codes & 0x07070707u;
+    const uint32_t sel = __byte_perm(lo3 | (lo3 >> 4), 0u, 0x4420u);  // 4 selector nibbles
+    const uint32_t a = __byte_perm(t[0], t[1], sel), b = __byte_perm(t[2], t[3], sel);
+    const uint32_t hi = ((codes >> 3) & 0x01010101u) * 0xFFu;         // codes 8..15
+    return (b & hi) | (a & ~hi);
+}
+
+// One warp per row (8 rows per CTA): no block-wide barrier, the row maximum
+// is a warp reduction, and every warp streams its row independently.
+__global__ void __launch_bounds__(kRowThreads) prep_w8_q4k_lut_kernel(const uint8_t* __restrict__ blocks, int k,
+                                                                       int n, int8_t* __restrict__ w,
+                                                                       float* __restrict__ scales,
+                                                                       int* __restrict__ err) {
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * (kRowThreads / 32) + (threadIdx.x >> 5);
+    if (row >= n) return;  // whole warps
+    const int nb = k >> 8, nsub = 8 * nb;
+    const uint8_t* src = blocks + static_cast<size_t>(row) * nb * 144;
+    float amax = 0.0f;
+    bool finite = true;
+#pragma unroll 4
+    for (int t = lane; t < nsub; t += 32) {
+        float d1, m1;
+        uint4 c0, c1;
+        int sh;
+        q4k_sub(src, t, d1, m1, c0, c1, sh);
+        const uint32_t m = 0x0F0F0F0Fu;
+        uint32_t lo = __vminu4(__vminu4(__vminu4((c0.x >> sh) & m, (c0.y >> sh) & m), (c0.z >> sh) & m),
+                               __vminu4(__vminu4((c0.w >> sh) & m, (c1.x >> sh) & m),
+                                        __vminu4(__vminu4((c1.y >> sh) & m, (c1.z >> sh) & m), (c1.w >> sh) & m)));
+        uint32_t hi = __vmaxu4(__vmaxu4(__vmaxu4((c0.x >> sh) & m, (c0.y >> sh) & m), (c0.z >> sh) & m),
+                               __vmaxu4(__vmaxu4((c0.w >> sh) & m, (c1.x >> sh) & m),
+                                        __vmaxu4(__vmaxu4((c1.y >> sh) & m, (c1.z >> sh) & m), (c1.w >> sh) & m)));
+        lo = __vminu4(lo, lo >> 16);
+        lo = min(lo & 0xFFu, (lo >> 8) & 0xFFu);
+        hi = __vmaxu4(hi, hi >> 16);
+        hi = max(hi & 0xFFu, (hi >> 8) & 0xFFu);
+        const float vlo = q4k_value(d1, m1, lo), vhi = q4k_value(d1, m1, hi);
+        finite &= isfinite(vlo) && isfinite(vhi);
+        amax = fmaxf(amax, fmaxf(fabsf(vlo), fabsf(vhi)));
+    }
+    if (__any_sync(0xffffffffu, !finite)) {
+        if (lane == 0) atomicExch(err, kErrNonFinite);
+        return;
+    }
+    const float scale = row_scale(warp_max(amax));
+    const float inv = row_inv(scale);
+    int8_t* dst = w + static_cast<size_t>(row) * k;
+#pragma unroll 2
+    for (int t = lane; t < nsub; t += 32) {
+        float d1, m1;
+        uint4 c0, c1;
+        int sh;
+        q4k_sub(src, t, d1, m1, c0, c1, sh);  // this warp's own loads: L1 hits
+        // the 16 possible values, quantised 4 at a time (quant_pack4: the
+        // same bytes as quant_value on each)
+        uint32_t tab[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            tab[i] = quant_pack4(make_float4(q4k_value(d1, m1, 4 * i), q4k_value(d1, m1, 4 * i + 1),
+                                             q4k_value(d1, m1, 4 * i + 2), q4k_value(d1, m1, 4 * i + 3)),
+                                 scale, inv);
+        const uint32_t m = 0x0F0F0F0Fu;
+        uint4 o0, o1;
+        o0.x = q4k_lookup4((c0.x >> sh) & m, tab);
+        o0.y = q4k_lookup4((c0.y >> sh) & m, tab);
+        o0.z = q4k_lookup4((c0.z >> sh) & m, tab);
+        o0.w = q4k_lookup4((c0.w >> sh) & m, tab);
+        o1.x = q4k_lookup4((c1.x >> sh) & m, tab);
+        o1.y = q4k_lookup4((c1.y >> sh) & m, tab);
+        o1.z = q4k_lookup4((c1.z >> sh) & m, tab);
+        o1.w = q4k_lookup4((c1.w >> sh) & m, tab);
+        uint4* out = reinterpret_cast<uint4*>(dst + 32 * static_cast<size_t>(t));
+        out[0] = o0;
+        out[1] = o1;
+    }
+    if (lane == 0) scales[row] = scale;
+}
+
 // FP16 route (dequantize_q*_k_prefill_f16, capi/src/lib.rs:393-455):
 // dequantise and round each value to f16; no finiteness check.
 template <int KIND>
@@ -478,6 +591,13 @@ bool launch_prep_reg(int bpw, const uint8_t* blocks, int k, int n, int8_t* w, fl
 
 void launch_prep_w8(int kind, const uint8_t* blocks, int k, int n, int8_t* w, float* scales, int* err,
                     cudaStream_t s) {
+    // Q4_K from 16-byte aligned blocks: one thread per sub-block, a warp per row (any k)
+    if (kind == kQ4K && (reinterpret_cast<uintptr_t>(blocks) & 15) == 0) {
+        const int rows_per_cta = kRowThreads / 32;
+        prep_w8_q4k_lut_kernel<<<(n + rows_per_cta - 1) / rows_per_cta, kRowThreads, 0, s>>>(blocks, k, n, w,
+                                                                                              scales, err);
+        return;
+    }
     // rows of up to 64 superblocks: the register kernel
     const int bpw = ((k >> 8) + 7) / 8;
     if (bpw <= 8) {

@@ -67,6 +67,48 @@ def test_prepare_golden_sidecar(dev):
         assert np.array_equal(_bits(s.cpu().numpy()), _bits(g[f"q{kind}_scale"]))
 
 
+@pytest.mark.parametrize("k,n", [(2048, 24), (24576, 6)])
+def test_prepare_q4k_edge_blocks_bit_exact(dev, rng, k, n):
+    """Q4_K preparation (one thread per sub-block, a 16-entry table per
+    sub-block, absmax from the smallest and largest code) against the oracle
+    on blocks where that could go wrong: one code repeated over a sub-block,
+    only codes 0 and 15, negative d and dmin, all-zero rows; k = 24576 takes
+    three passes per row.  The same blocks 4 bytes past a 16-byte boundary
+    take the other kernel (which needs 4-byte alignment only) and must give
+    the same bytes."""
+    nb = k // 256
+    blocks = random_kquant_blocks(4, n * nb, rng).reshape(n, nb, 144)
+    half = lambda v: np.array([v], dtype=np.float16).view(np.uint8)
+    for r in range(n):
+        for b in range(nb):
+            mode = (r + b) % 4
+            if mode == 0:  # every sub-block one repeated code
+                for c in range(4):
+                    blocks[r, b, 16 + 32 * c:48 + 32 * c] = rng.integers(0, 16) * 17
+            elif mode == 1:  # only the extreme codes
+                blocks[r, b, 16:] = rng.choice([0x00, 0x0F, 0xF0, 0xFF], size=128)
+            elif mode == 2:  # negative scales
+                blocks[r, b, 0:2] = half(-rng.uniform(1e-3, 2e-2))
+                blocks[r, b, 2:4] = half(-rng.uniform(1e-3, 2e-2))
+    blocks[n - 1] = 0  # an all-zero row: scale 1.0
+    blocks = np.ascontiguousarray(blocks.reshape(-1))
+    st, w_ref, s_ref = oracle.prepare_w8a8(4, blocks, k, n)
+    assert st == 0
+    status = dev.new_status()
+    w, s = dev.prepare_w8(4, torch.from_numpy(blocks).cuda(), k, n, status)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    assert np.array_equal(w.cpu().numpy(), w_ref)
+    assert np.array_equal(_bits(s.cpu().numpy()), _bits(s_ref))
+    shifted = torch.zeros(blocks.size + 16, dtype=torch.uint8, device="cuda")
+    shifted[4:4 + blocks.size] = torch.from_numpy(blocks).cuda()
+    assert shifted[4:].data_ptr() % 16 == 4
+    w2, s2 = dev.prepare_w8(4, shifted[4:4 + blocks.size], k, n, status)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    assert np.array_equal(w2.cpu().numpy(), w_ref) and np.array_equal(_bits(s2.cpu().numpy()), _bits(s_ref))
+
+
 def test_prepare_flags_non_finite(dev):
     blk = np.zeros(144, dtype=np.uint8)
     blk[0:2] = np.array([np.inf], dtype=np.float16).view(np.uint8)
