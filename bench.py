@@ -1149,6 +1149,31 @@ def cfg5_block(ms_list, steps, warmup, rank, world, route="peer", check=True):
                                "hbm_frac": round(q6bytes / (q6_ms * 1e-3) / 1e9 / hbm_peak, 4),
                                "bytes": q6bytes}
             del layout, yq
+            # K1 on the same rows (once per weight, at load time): Q4_K and
+            # Q6_K blocks -> int8 rows + per-row scales
+            pw = torch.empty((width, CFG5_K), dtype=torch.int8, device="cuda")
+            ps = torch.empty(width, dtype=torch.float32, device="cuda")
+            pst = dev.new_status()
+            for kind, hb, bb, name in ((4, blocks, 144, "prep_q4k"), (6, blocks6, 210, "prep_q6k")):
+                db = torch.from_numpy(hb).cuda()
+
+                def prep(kind=kind, db=db):
+                    return rk.lib().rocknpu_b200_prepare_w8(kind, db.data_ptr(), CFG5_K, width, pw.data_ptr(),
+                                                            ps.data_ptr(), pst.data_ptr(),
+                                                            torch.cuda.current_stream().cuda_stream)
+
+                p_ms = _timed(prep, max(steps, 10), warmup, dist)
+                torch.cuda.synchronize()
+                assert pst.item() == 0, "prepare_w8 status error"
+                pbytes = width * (CFG5_K // 256) * bb + width * CFG5_K + 4 * width
+                res[name] = {"kernel": "prep_w8_q4k_lut_kernel (a thread per sub-block, 16-entry byte tables)"
+                             if kind == 4 else "prep_w8_reg_kernel (dequantise in registers, absmax, int8)",
+                             "us_local": round(p_ms * 1e3, 1),
+                             "gbs_local": round(pbytes / (p_ms * 1e-3) / 1e9, 1),
+                             "hbm_frac": round(pbytes / (p_ms * 1e-3) / 1e9 / hbm_peak, 4),
+                             "bytes": pbytes}
+                del db
+            del pw, ps
         for m in ms_list:
             x = cfg5_activations(m)
             ms = _timed(lambda: sm(x), steps, warmup, dist)
