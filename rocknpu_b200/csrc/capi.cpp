@@ -295,10 +295,10 @@ struct RockNpuContext {
     DevBuf gemm_ws;      // split-K workspace, all-zero between launches
     DevBuf quant_sync;   // fused-quantiser counters, all-zero between launches
     DevBuf hilo_a, hilo_out;  // HILO stacked activations [2m][k], summed outputs
-    // M=1 staging, device and page-locked host blocks with one layout,
-    // [y: outputs][status word, 16 bytes][x: k floats]: a call copies the
-    // zeroed status word and x in with one copy, and y with the status out
-    // with one copy (m1_call).
+    // M=1 staging (m1_call): a page-locked, device-mapped host block
+    // [y: outputs][status word, 16 bytes][x: k floats] that the kernels write
+    // y and the status into, and a device block of the same layout whose x
+    // part receives the one copy of a call.
     DevBuf m1_dev;
     HostBuf m1_host;
     bool in_hilo = false;     // inside a HILO-encoded call (HiloInner, L:2025-2043)
@@ -548,21 +548,18 @@ void zero_copy_mode(bool* in, bool* out) {
     }
 }
 
-// One M=1 call from host buffers, for both decode routes: x and a zeroed
-// status word go in with one copy from the page-locked staging block, the
-// kernels queued by `launch(x, y, err)` run on c->stream, y and the status
-// come back with one copy, and the host waits once.  Each copy or memset in
-// a stream costs the call a few microseconds on B200, so the sequence has
-// three operations (copy, kernels, copy) where the general path has seven.
-// On an error the caller's outputs are untouched; a non-finite x is
-// INVALID_ARGUMENT, as on the general path.
-//
-// host_out: the kernels write y and the status word straight into the
-// page-locked block through its device mapping (plain stores; see
-// launch_gemv_w8a8_x), so only x is copied and there is no output copy.
+// One M=1 call from host buffers, for both decode routes.  The host zeroes
+// the status word and writes x into the page-locked, device-mapped staging
+// block; one copy moves x to the device, and the kernels queued by
+// `launch(x, y, err)` on c->stream write y and any error straight into the
+// host block through its mapping (plain stores: launch_gemv_w8a8_x,
+// kq::set_err); the host waits once.  Each copy or memset in a stream costs a
+// call a few microseconds on B200, so the sequence has two operations (copy,
+// kernels) where the general path has seven.  On an error the caller's
+// outputs are untouched; a non-finite x is INVALID_ARGUMENT, as on the
+// general path.
 template <class Launch>
-int m1_call(Ctx* c, const float* a, size_t k, const OutSeg* segs, size_t nseg, bool overlap, bool host_out,
-            Launch&& launch) {
+int m1_call(Ctx* c, const float* a, size_t k, const OutSeg* segs, size_t nseg, bool overlap, Launch&& launch) {
     size_t total = 0;
     for (size_t i = 0; i < nseg; ++i) total += segs[i].n;
     const size_t y_bytes = round_up(total * sizeof(float), 16);
@@ -574,15 +571,11 @@ int m1_call(Ctx* c, const float* a, size_t k, const OutSeg* segs, size_t nseg, b
     int* h_st = reinterpret_cast<int*>(hb + y_bytes);
     std::memset(h_st, 0, 16);
     std::memcpy(hb + y_bytes + 16, a, k * sizeof(float));
-    const size_t in_off = host_out ? y_bytes + 16 : y_bytes;  // the status word travels only without host_out
-    if (cudaMemcpyAsync(db + in_off, hb + in_off, bytes - in_off, cudaMemcpyHostToDevice, c->stream))
+    if (cudaMemcpyAsync(db + y_bytes + 16, hb + y_bytes + 16, k * sizeof(float), cudaMemcpyHostToDevice, c->stream))
         return kExecError;
-    const cudaError_t le =
-        host_out ? launch(reinterpret_cast<const float*>(db + y_bytes + 16), reinterpret_cast<float*>(hd),
-                          reinterpret_cast<int*>(hd + y_bytes))
-                 : launch(reinterpret_cast<const float*>(db + y_bytes + 16), reinterpret_cast<float*>(db),
-                          reinterpret_cast<int*>(db + y_bytes));
-    if (le != cudaSuccess) return kExecError;
+    if (launch(reinterpret_cast<const float*>(db + y_bytes + 16), reinterpret_cast<float*>(hd),
+               reinterpret_cast<int*>(hd + y_bytes)) != cudaSuccess)
+        return kExecError;
     if (overlap && c->overlap) {
         // one-shot host work while the GPU runs (take_overlap, L:264-273)
         rocknpu_overlap_fn fn = c->overlap;
@@ -591,8 +584,6 @@ int m1_call(Ctx* c, const float* a, size_t k, const OutSeg* segs, size_t nseg, b
         c->overlap_user = nullptr;
         fn(user);
     }
-    if (!host_out && cudaMemcpyAsync(hb, db, y_bytes + 16, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
-        return kExecError;
     if (wait_stream(c->stream) != cudaSuccess) return kExecError;
     const int s = *h_st;
     if (s != rk::kErrNone) return s == rk::kErrNonFinite ? kInvalid : kExecError;
@@ -620,12 +611,11 @@ int run_w8a8(Ctx* c, const PreparedW8& pw, const float* host_a, size_t m, size_t
     const size_t total_n = pw.n;
     if (m == 1 && k % 16 == 0 && !dev_a) {
         // K2 + K5 fused into one launch (the row quantiser's bits)
-        return m1_call(c, host_a, k, segs, nseg, m1_overlap, /*host_out=*/true,
-                       [&](const float* x, float* y, int* err) {
-                           rk::launch_gemv_w8a8_x(pw.w, pw.scales, x, static_cast<int>(k), static_cast<int>(total_n),
-                                                  y, err, c->stream, /*host_out=*/true);
-                           return cudaGetLastError();
-                       });
+        return m1_call(c, host_a, k, segs, nseg, m1_overlap, [&](const float* x, float* y, int* err) {
+            rk::launch_gemv_w8a8_x(pw.w, pw.scales, x, static_cast<int>(k), static_cast<int>(total_n), y, err,
+                                   c->stream, /*host_out=*/true);
+            return cudaGetLastError();
+        });
     }
     if ((!dev_a && c->a_f32.ensure(m * k * sizeof(float))) || c->a_i8.ensure(m * ld8) ||
         c->a_scale.ensure(m * sizeof(float)) || c->out_f32.ensure(m * total_n * sizeof(float)))
@@ -948,7 +938,7 @@ int decode_kq_m1(Ctx* c, const KeyList& keys, const Member* members, size_t coun
     if (!hit) c->m1_shapes.insert({k, total});
     OutSeg osegs[4];
     for (size_t t = 0; t < n_order; ++t) osegs[t] = segs[order[t]];
-    const int st = m1_call(c, a, k, osegs, count, true, /*host_out=*/true, [&](const float* x, float* y, int* err) {
+    const int st = m1_call(c, a, k, osegs, count, true, [&](const float* x, float* y, int* err) {
         for (int g = 0; g < ngroups; ++g) {
             const int e = rk::launch_gemv_kq(p[g]->kind, p[g]->layout, static_cast<int>(k), static_cast<int>(p[g]->n),
                                              x, y, err, c->stream, /*host_out=*/true);
