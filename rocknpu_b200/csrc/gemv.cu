@@ -23,31 +23,57 @@ __device__ __forceinline__ int4 ld_stream(const int4* p) {
     return v;
 }
 
+// The first chunks a lane reads of its warp's row (16-byte chunks lane,
+// lane + 32, lane + 64, lane + 96; zero past the row or for a row past n),
+// issued before the activation is ready so that their DRAM latency overlaps
+// its staging; at k <= 2048 they are the whole row.
+__device__ __forceinline__ void row_head(const int8_t* __restrict__ w, int k, int n, int4 (&pre)[4]) {
+    const int chunks = k >> 4;
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
+    const int4* wr = reinterpret_cast<const int4*>(w + static_cast<size_t>(row) * k);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const int idx = lane + 32 * u;
+        pre[u] = (row < n && idx < chunks) ? ld_stream(wr + idx) : make_int4(0, 0, 0, 0);
+    }
+}
+
+__device__ __forceinline__ int dot_chunk(const int4& w, const int4& a, int acc) {
+    acc = __dp4a(w.x, a.x, acc);
+    acc = __dp4a(w.y, a.y, acc);
+    acc = __dp4a(w.z, a.z, acc);
+    return __dp4a(w.w, a.w, acc);
+}
+
 // The warp's row of this CTA against the quantised activation staged in
-// shared memory: the rescaled result, in every lane (0 for a row past n).
+// shared memory, starting from its row_head: the rescaled result, in every
+// lane (0 for a row past n).  The int32 sum is exact, so the order in which
+// chunks are added does not change it.
 __device__ __forceinline__ float gemv_row(const int4* sa, const int8_t* __restrict__ w,
-                                          const float* __restrict__ w_scale, float a_scale, int k, int n) {
+                                          const float* __restrict__ w_scale, float a_scale, int k, int n,
+                                          const int4 (&pre)[4]) {
     const int chunks = k >> 4;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * kRowsPerCta + warp;
     if (row >= n) return 0.0f;
     const int4* wr = reinterpret_cast<const int4*>(w + static_cast<size_t>(row) * k);
     int acc = 0;
-    int i = lane;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const int idx = lane + 32 * u;
+        if (idx < chunks) acc = dot_chunk(pre[u], sa[idx], acc);
+    }
+    int i = lane + 128;
     for (; i + 96 < chunks; i += 128) {
         const int4 w0 = ld_stream(wr + i), w1 = ld_stream(wr + i + 32), w2 = ld_stream(wr + i + 64),
                    w3 = ld_stream(wr + i + 96);
-        const int4 a0 = sa[i], a1 = sa[i + 32], a2 = sa[i + 64], a3 = sa[i + 96];
-        acc = __dp4a(w0.x, a0.x, acc); acc = __dp4a(w0.y, a0.y, acc); acc = __dp4a(w0.z, a0.z, acc); acc = __dp4a(w0.w, a0.w, acc);
-        acc = __dp4a(w1.x, a1.x, acc); acc = __dp4a(w1.y, a1.y, acc); acc = __dp4a(w1.z, a1.z, acc); acc = __dp4a(w1.w, a1.w, acc);
-        acc = __dp4a(w2.x, a2.x, acc); acc = __dp4a(w2.y, a2.y, acc); acc = __dp4a(w2.z, a2.z, acc); acc = __dp4a(w2.w, a2.w, acc);
-        acc = __dp4a(w3.x, a3.x, acc); acc = __dp4a(w3.y, a3.y, acc); acc = __dp4a(w3.z, a3.z, acc); acc = __dp4a(w3.w, a3.w, acc);
+        acc = dot_chunk(w0, sa[i], acc);
+        acc = dot_chunk(w1, sa[i + 32], acc);
+        acc = dot_chunk(w2, sa[i + 64], acc);
+        acc = dot_chunk(w3, sa[i + 96], acc);
     }
-    for (; i < chunks; i += 32) {
-        const int4 w0 = ld_stream(wr + i);
-        const int4 a0 = sa[i];
-        acc = __dp4a(w0.x, a0.x, acc); acc = __dp4a(w0.y, a0.y, acc); acc = __dp4a(w0.z, a0.z, acc); acc = __dp4a(w0.w, a0.w, acc);
-    }
+    for (; i < chunks; i += 32) acc = dot_chunk(ld_stream(wr + i), sa[i], acc);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     return __fmul_rn(__fmul_rn(__int2float_rn(acc), a_scale), w_scale[row]);
@@ -59,10 +85,12 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_w8a8_kernel(const int8_t* _
                                                                   const float* __restrict__ a_scale, int k, int n,
                                                                   float* __restrict__ out) {
     extern __shared__ int4 sa[];
+    int4 pre[4];
+    row_head(w, k, n, pre);
     const int chunks = k >> 4;
     for (int i = threadIdx.x; i < chunks; i += kGemvThreads) sa[i] = reinterpret_cast<const int4*>(a8)[i];
     __syncthreads();
-    const float v = gemv_row(sa, w, w_scale, *a_scale, k, n);
+    const float v = gemv_row(sa, w, w_scale, *a_scale, k, n, pre);
     const int row = blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
     if ((threadIdx.x & 31) == 0 && row < n) out[row] = v;
 }
@@ -84,6 +112,8 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_w8a8_x_kernel(const int8_t*
                                                                     float* __restrict__ out, int* err) {
     extern __shared__ int4 sa[];
     __shared__ float red[kGemvThreads / 32];
+    int4 pre[4];
+    row_head(w, k, n, pre);
     const float4* x4 = reinterpret_cast<const float4*>(x);
     const int k4 = k >> 2;
     float amax = 0.0f;
@@ -112,7 +142,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_w8a8_x_kernel(const int8_t*
     uint32_t* sa32 = reinterpret_cast<uint32_t*>(sa);
     for (int i = threadIdx.x; i < k4; i += kGemvThreads) sa32[i] = quant_pack4(__ldg(x4 + i), scale, inv);
     __syncthreads();
-    const float v = gemv_row(sa, w, w_scale, scale, k, n);
+    const float v = gemv_row(sa, w, w_scale, scale, k, n, pre);
     if constexpr (HostOut) {
         __shared__ float res[kRowsPerCta];
         if ((threadIdx.x & 31) == 0) res[threadIdx.x >> 5] = v;
