@@ -81,6 +81,7 @@ def test_device_entry_points_reject_bad_arguments():
     L = rk.lib()
     assert L.rocknpu_b200_prepare_w8(7, None, 256, 1, None, None, None, None) == -1
     assert L.rocknpu_b200_prepare_w8(4, 1, 100, 1, 1, 1, 1, None) == -1  # k % 256
+    assert L.rocknpu_b200_prepare_w8(4, 4098, 256, 1, 16, 16, 16, None) == -1  # blocks not 4-byte aligned
     assert L.rocknpu_b200_quantize_rows(None, 1, 1, None, 1, None, None, None) == -1
     assert L.rocknpu_b200_gemm_w8a8(None, 0, None, None, 0, None, None, 0, None, 1, 1, 1, None, 0, None, None) == -1
     assert L.rocknpu_b200_gemv_w8a8(1, 1, 1, 1, 1, 100, 4, None) == -1  # k % 16
